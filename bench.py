@@ -1,0 +1,599 @@
+"""Benchmark of the B200 attention backend (one JSON line on rank 0).
+
+Default workload (``--workload c5``): BASELINE configs[4], Gemma-3-270M-shaped
+decode, batch 256 sequences per GPU, 4 query heads / 1 kv head, head_dim 256,
+fp16 KV cache, context lengths ~ U[1024, 32768].  One step = one decode token
+per sequence through one sliding-window-512 local layer (RoPE theta 1e4) and
+one global layer (theta 1e6), each with per-head zero-centred RMS QK-norm,
+i.e. two ``b2a_decode`` calls on two separate caches.  ``value`` is decode
+tokens/s over all ranks (weak scaling: every rank owns its own 256 sequences,
+no collective in the timed region).  ``e2e`` is the same step through the C ABI
+with the step's inputs (new q/k/v, context lengths) copied from pinned host
+memory and the outputs copied back inside the timed region; the KV caches are
+device-resident state, as in the reference's GPU-resident decode.
+
+Other workloads: c1 (SmolLM2 prefill, fp32), c2 (MiniLM encoder, fp16),
+c3 (Qwen2.5 decode, fp16 cache), c4 (Phi-3 prefill, bf16).  At N=1 rank 0 also
+times c1-c4 once and reports them under ``suite``.
+
+``--impl reference`` times the CPU restatement of the reference's Java CPU
+attention (the oracle, OpenMP over all host threads) on a bounded sample of
+the same workload; the reference itself (Java 21) cannot run on this machine.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "win-directml-java_b200"))
+sys.path.insert(0, REPO)
+
+MEASURED_PEAKS = os.path.join(REPO, "MEASURED_PEAKS.json")
+FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
+
+WORKLOADS = {
+    "c1": "SmolLM2-135M causal prefill B1 S256 9/3 D64 fp32 (configs[0])",
+    "c2": "MiniLM-L6 encoder B64 S128 H12 D32 fp16 key-padding (configs[1])",
+    "c3": "Qwen2.5-0.5B decode B64 14/2 D64 fp16 KV ctx~U[512,8192] (configs[2])",
+    "c4": "Phi-3-mini causal prefill B8 S4096 H32 D96 bf16 (configs[3])",
+    "c5": "Gemma-3-270M decode B256 4/1 D256 local W512 + global, QK-norm, fp16 KV ctx~U[1024,32768] (configs[4])",
+}
+
+
+def peaks():
+    try:
+        with open(MEASURED_PEAKS) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), float(m["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class NvmlClockSampler:
+    """Reads SM clock and clock-event reasons through NVML every 5 ms in a thread
+    (read-only queries; nothing is changed on the GPU)."""
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, gpu_index: int):
+        import threading
+        self.gpu, self.samples, self.reasons = gpu_index, [], set()
+        self.stop = threading.Event()
+        self.thread = None
+        self.max_mhz = None
+        self.ok = False
+
+    def _run(self, nv, h):
+        while not self.stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self.stop.wait(0.005)
+
+    def __enter__(self):
+        import threading
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            idx = self.gpu
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            if vis:
+                try:
+                    idx = int(vis.split(",")[self.gpu])
+                except (ValueError, IndexError):
+                    pass
+            h = nv.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._run, args=(nv, h), daemon=True)
+            self.thread.start()
+            self.ok = True
+        except Exception:
+            self.ok = False
+        return self
+
+    def __exit__(self, *exc):
+        self.stop.set()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return None
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": sorted(self.reasons), "source": "nvml 5 ms"}
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"b2a_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------------ workloads
+class DecodeWorkload:
+    """configs[4] (c5) or configs[2] (c3): one decode token for every sequence."""
+
+    def __init__(self, name: str, seed: int, batch: int = 0):
+        import torch
+        import b200attn
+        self.torch, self.b2a = torch, b200attn
+        if name == "c5":
+            self.B, self.Hq, self.Hkv, self.D, self.lo, self.hi = 256, 4, 1, 256, 1024, 32768
+            self.layers = [dict(window=512, theta=1e4), dict(window=0, theta=1e6)]
+            self.layout, self.rope, self.norm = b200attn.KV_POS_MAJOR, b200attn.ROPE_GEMMA, True
+        else:
+            self.B, self.Hq, self.Hkv, self.D, self.lo, self.hi = 64, 14, 2, 64, 512, 8192
+            self.layers = [dict(window=0, theta=1e6)]
+            self.layout, self.rope, self.norm = b200attn.KV_HEAD_MAJOR, b200attn.ROPE_NEOX, False
+        if batch > 0:  # smaller batch for profiler captures only
+            self.B = batch
+        import oracle
+        self.lens = oracle.splitmix_uniform_int(seed, self.B, self.lo, self.hi)
+        self.max_seq = self.hi + 1
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        B, Hq, Hkv, D, S = self.B, self.Hq, self.Hkv, self.D, self.max_seq
+        shape = (B, Hkv, S, D) if self.layout == b200attn.KV_HEAD_MAJOR else (B, S, Hkv, D)
+        self.caches = []
+        for _ in self.layers:
+            kc = torch.empty(shape, dtype=torch.float16, device="cuda")
+            vc = torch.empty(shape, dtype=torch.float16, device="cuda")
+            for t in (kc, vc):
+                for b in range(B):  # per-sequence slices keep the fp32 temporaries small
+                    t[b].normal_(generator=g)
+            self.caches.append((kc, vc))
+        mk = lambda *s: torch.randn(*s, generator=g, device="cuda").to(torch.float16)
+        self.q = [mk(B, Hq, D) for _ in self.layers]
+        self.kn = [mk(B, Hkv, D) for _ in self.layers]
+        self.vn = [mk(B, Hkv, D) for _ in self.layers]
+        self.qw = torch.randn(D, generator=g, device="cuda") * 0.5 if self.norm else None
+        self.kw = torch.randn(D, generator=g, device="cuda") * 0.5 if self.norm else None
+        self.lens_d = torch.from_numpy(self.lens).cuda()
+        self.out = [torch.empty(B, Hq, D, device="cuda") for _ in self.layers]
+        self.scale = 1.0 / math.sqrt(D)
+        # host-side mirrors for the end-to-end arm
+        pin = lambda t: t.cpu().pin_memory()
+        self.h_q = [pin(t) for t in self.q]
+        self.h_kn = [pin(t) for t in self.kn]
+        self.h_vn = [pin(t) for t in self.vn]
+        self.h_lens = pin(self.lens_d)
+        self.h_out = [torch.empty(B, Hq, D).pin_memory() for _ in self.layers]
+
+    def tokens_per_step(self):
+        return self.B
+
+    def kernel_launches_per_step(self):
+        return len(self.layers)
+
+    def algorithmic_bytes(self):
+        """KV bytes each decode launch must read + new rows written + q/o/new k/v, summed over the step."""
+        total = 0
+        for layer in self.layers:
+            L = self.lens.astype(np.int64)
+            visible = np.minimum(L + 1, layer["window"]) if layer["window"] > 0 else L + 1
+            kv = int(visible.sum()) * self.Hkv * self.D * 2 * 2
+            small = self.B * (self.Hq + 2 * self.Hkv) * self.D * 2 + self.B * self.Hq * self.D * 4
+            total += kv + small + self.B * self.Hkv * self.D * 2 * 2
+        return total
+
+    def flops(self):
+        total = 0
+        for layer in self.layers:
+            L = self.lens.astype(np.int64)
+            visible = np.minimum(L + 1, layer["window"]) if layer["window"] > 0 else L + 1
+            total += int(visible.sum()) * self.Hq * self.D * 4
+        return total
+
+    def launch(self, ctx, i, stream=None):
+        layer = self.layers[i]
+        kc, vc = self.caches[i]
+        self.b2a.decode(ctx, self.q[i], self.kn[i], self.vn[i], kc, vc, self.lens_d, self.out[i], self.scale,
+                        kv_layout=self.layout, rope_mode=self.rope, rope_theta=layer["theta"],
+                        window=layer["window"], q_norm_w=self.qw, k_norm_w=self.kw, norm_eps=1e-6, stream=stream)
+
+    def step(self, ctx, stream=None):
+        for i in range(len(self.layers)):
+            self.launch(ctx, i, stream)
+
+    def step_e2e(self, ctx, stream=None):
+        self.lens_d.copy_(self.h_lens, non_blocking=True)
+        for i in range(len(self.layers)):
+            self.q[i].copy_(self.h_q[i], non_blocking=True)
+            self.kn[i].copy_(self.h_kn[i], non_blocking=True)
+            self.vn[i].copy_(self.h_vn[i], non_blocking=True)
+            self.launch(ctx, i, stream)
+            self.h_out[i].copy_(self.out[i], non_blocking=True)
+
+    def e2e_bytes(self):
+        h2d = self.lens.nbytes + sum(t.numel() * t.element_size() for t in self.h_q + self.h_kn + self.h_vn)
+        d2h = sum(t.numel() * t.element_size() for t in self.h_out)
+        return h2d, d2h
+
+    def config(self):
+        return {"batch_per_gpu": self.B, "q_heads": self.Hq, "kv_heads": self.Hkv, "head_dim": self.D,
+                "ctx_len": f"U[{self.lo},{self.hi}]", "mean_ctx": float(self.lens.mean()),
+                "layers_per_step": [("local W%d" % l["window"]) if l["window"] else "global" for l in self.layers],
+                "kv_dtype": "f16", "l2": "inputs larger than L2 (KV caches %.1f GB)" % (
+                    sum(t.numel() * 2 for c in self.caches for t in c) / 1e9)}
+
+
+class PrefillWorkload:
+    """c1 / c4: causal prefill with fused RoPE; c2: masked encoder."""
+
+    def __init__(self, name: str, seed: int):
+        import torch
+        import b200attn
+        import oracle
+        self.torch, self.b2a, self.name = torch, b200attn, name
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        if name == "c1":
+            self.B, self.S, self.Hq, self.Hkv, self.D, self.dt, self.theta = 1, 256, 9, 3, 64, torch.float32, 1e5
+        elif name == "c4":
+            self.B, self.S, self.Hq, self.Hkv, self.D, self.dt, self.theta = 8, 4096, 32, 32, 96, torch.bfloat16, 1e4
+        else:
+            self.B, self.S, self.Hq, self.Hkv, self.D, self.dt, self.theta = 64, 128, 12, 12, 32, torch.float16, 0
+            self.lens = oracle.splitmix_uniform_int(seed, self.B, 16, 128)
+            self.lens_d = torch.from_numpy(self.lens).cuda()
+        mk = lambda h: torch.randn(self.B, self.S, h, self.D, generator=g, device="cuda").to(self.dt)
+        self.q, self.k, self.v = mk(self.Hq), mk(self.Hkv), mk(self.Hkv)
+        self.o = torch.empty_like(self.q)
+        self.scale = 1.0 / math.sqrt(self.D)
+
+    def tokens_per_step(self):
+        return self.B * self.S
+
+    def kernel_launches_per_step(self):
+        return 1 if self.name == "c2" else 4  # rope table, rope q, rope k, attention
+
+    def flops(self):
+        if self.name == "c2":
+            return 4 * self.Hq * self.D * self.S * int(self.lens.astype(np.int64).sum())
+        return 4 * self.B * self.Hq * self.D * self.S * (self.S + 1) // 2
+
+    def algorithmic_bytes(self):
+        e = self.q.element_size()
+        return e * self.B * self.S * self.D * (2 * self.Hq + 2 * self.Hkv)
+
+    def step(self, ctx, stream=None):
+        if self.name == "c2":
+            self.b2a.mha(ctx, self.q, self.k, self.v, self.o, self.scale, key_lengths=self.lens_d,
+                         layout=self.b2a.SEQ_MAJOR, stream=stream)
+        else:
+            self.b2a.prefill_causal(ctx, self.q, self.k, self.v, self.o, self.scale, rope_mode=self.b2a.ROPE_NEOX,
+                                    rope_theta=self.theta, stream=stream)
+
+
+def time_steps(torch, fn, steps, flush=None):
+    """Per-step CUDA-event durations (ms) on the current stream."""
+    s = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in evs:
+        if flush is not None:
+            flush()
+        a.record(s)
+        fn()
+        b.record(s)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def run_suite(ctx, hbm, tflops, src):
+    import torch
+    flush_buf = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    flush = lambda: flush_buf.fill_(1.0)
+    out = {}
+    for name in ("c1", "c2", "c3", "c4"):
+        w = DecodeWorkload(name, 3) if name == "c3" else PrefillWorkload(name, {"c1": 1, "c2": 2, "c4": 4}[name])
+        for _ in range(3):
+            w.step(ctx)
+        torch.cuda.synchronize()
+        ms = statistics.mean(time_steps(torch, lambda: w.step(ctx), 10, flush))
+        entry = {"workload": WORKLOADS[name], "ms": round(ms, 4),
+                 "tokens_per_s": round(w.tokens_per_step() / (ms / 1e3), 1)}
+        gbs = w.algorithmic_bytes() / (ms / 1e3) / 1e9
+        tfs = w.flops() / (ms / 1e3) / 1e12
+        entry["hbm_gbs"] = round(gbs, 1)
+        entry["hbm_frac"] = round(gbs / hbm, 4)
+        entry["tflops"] = round(tfs, 2)
+        entry["tensor_frac"] = round(tfs / tflops, 4)
+        entry["bound"] = "tensor" if name == "c4" else "hbm"
+        entry["peak_source"] = src
+        out[name] = entry
+        del w
+        torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------------ CPU reference arm
+class CpuDecodeSample:
+    """n_seq sequences of the c5 workload held as float32 arrays for the CPU
+    restatement (OpenMP over all host threads); one step = local + global layer."""
+
+    def __init__(self, n_seq: int, seed: int = 5):
+        import oracle
+        self.oracle = oracle
+        self.n = n_seq
+        self.lens = oracle.splitmix_uniform_int(seed, 256, 1024, 32768)[:n_seq].astype(np.int32)
+        self.D, self.Hq, self.Hkv = 256, 4, 1
+        self.max_seq = int(self.lens.max()) + 1
+        rng = np.random.default_rng(seed)
+        shape = (n_seq, self.Hkv, self.max_seq, self.D)
+        self.caches = []
+        for _ in range(2):  # one cache per layer, as on the GPU
+            kc = oracle.round_to(rng.standard_normal(shape, dtype=np.float32), oracle.F16).reshape(shape)
+            vc = oracle.round_to(rng.standard_normal(shape, dtype=np.float32), oracle.F16).reshape(shape)
+            self.caches.append((kc, vc))
+        r = lambda *s: oracle.round_to(rng.standard_normal(s, dtype=np.float32), oracle.F16).reshape(s)
+        self.q, self.kn, self.vn = r(n_seq, self.Hq, self.D), r(n_seq, self.Hkv, self.D), r(n_seq, self.Hkv, self.D)
+        self.w = (0.5 * rng.standard_normal(self.D)).astype(np.float32)
+        self.threads = oracle.max_threads()
+
+    def step(self):
+        o = self.oracle
+        for (kc, vc), (window, theta) in zip(self.caches, ((512, 1e4), (0, 1e6))):
+            o.decode(self.q, self.kn, self.vn, kc, vc, self.lens, B=self.n, Hq=self.Hq, Hkv=self.Hkv, D=self.D,
+                     max_seq=self.max_seq, scale=1 / 16, rope_theta=theta, rope_mode=o.ROPE_GEMMA, window=window,
+                     cache_layout=o.KV_HEAD_MAJOR, q_norm_w=self.w, k_norm_w=self.w,
+                     softmax_mode=o.SOFTMAX_GEMMA, n_threads=self.threads, inplace=True)
+
+
+def cpu_decode_sample(n_seq: int, max_seconds: float = 12.0):
+    """Times the CPU restatement on a bounded sample; returns (tokens/s, threads, seconds, steps)."""
+    smp = CpuDecodeSample(n_seq)
+    smp.step()  # warm caches / thread pool
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        smp.step()
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= max_seconds or steps >= 200:
+            break
+    return n_seq * steps / el, smp.threads, el, steps
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import oracle
+    oracle.build()
+    n_seq = 8
+    smp = CpuDecodeSample(n_seq)
+    for _ in range(args.warmup):
+        smp.step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        smp.step()
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.mean(times)
+    value = n_seq / (ms / 1e3)
+    threads = oracle.max_threads()
+    sample = f"{n_seq} of 256 sequences of {WORKLOADS['c5']}, one local + one global layer per step"
+    line = {"metric": "decode tokens/s", "value": round(value, 3), "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": WORKLOADS["c5"], "sample": sample},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": sample + "; C restatement of the reference's Java CPU attention "
+                                                "(no JDK on this machine)"},
+            "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ main arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="c5", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-suite", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0, help="override the decode batch (profiling captures only)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+    import b200attn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    if not os.path.exists(b200attn.LIB_PATH):
+        if rank == 0:
+            b200attn.build()
+        if world > 1:
+            dist.barrier()
+    ctx = b200attn.Context(local)
+    hbm, tflops, src = peaks()
+
+    w = DecodeWorkload(args.workload, 5 + rank, args.batch) if args.workload in ("c3", "c5") else \
+        PrefillWorkload(args.workload, {"c1": 1, "c2": 2, "c4": 4}[args.workload])
+    for _ in range(args.warmup):
+        w.step(ctx)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-resident timed region
+    s = torch.cuda.current_stream()
+    per_launch = []
+    barrier()
+    with NvmlClockSampler(local) as clk, ClockSampler(local) as clk_smi:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(s)
+        if isinstance(w, DecodeWorkload):
+            evs = []
+            for _ in range(args.steps):
+                for i in range(len(w.layers)):
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record(s)
+                    w.launch(ctx, i)
+                    b.record(s)
+                    evs.append((a, b))
+        else:
+            evs = []
+            for _ in range(args.steps):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(s)
+                w.step(ctx)
+                b.record(s)
+                evs.append((a, b))
+        t1.record(s)
+        barrier()
+    elapsed_ms = t0.elapsed_time(t1)
+    per_launch = [a.elapsed_time(b) for a, b in evs]
+    clocks = clk.summary() or clk_smi.summary()
+
+    # ---- end-to-end timed region (host buffers, copies inside)
+    if isinstance(w, DecodeWorkload):
+        for _ in range(2):
+            w.step_e2e(ctx)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(args.steps):
+            w.step_e2e(ctx)
+        e1.record(s)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1)
+        h2d, d2h = w.e2e_bytes()
+    else:
+        e2e_ms, h2d, d2h = elapsed_ms, 0, 0
+
+    # max over ranks (device-timed)
+    t = torch.tensor([elapsed_ms, e2e_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+    ms_step = elapsed_ms / args.steps
+    tokens = w.tokens_per_step() * world
+    value = tokens / (ms_step / 1e3)
+    e2e_value = tokens / (e2e_ms / args.steps / 1e3)
+
+    # roofline of the dominant kernel (decode: the split-KV kernel; bytes summed over launches)
+    kern_ms = sum(per_launch)
+    if isinstance(w, DecodeWorkload):
+        achieved = w.algorithmic_bytes() * args.steps / (kern_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "peak_source": src + " (hbm_gbs, burst copy)",
+                "kernel": "decode_tc_kernel<256,half>" if args.workload == "c5" else "decode_tc_kernel<64,half>",
+                "bytes_per_step": w.algorithmic_bytes(), "traffic": None,
+                "per_layer_ms": [round(statistics.mean(per_launch[i::len(w.layers)]), 4)
+                                 for i in range(len(w.layers))]}
+    else:
+        achieved = w.flops() * args.steps / (kern_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tflops, "unit": "TFLOP/s",
+                "frac": round(achieved / tflops, 4), "peak_source": src + " (bf16_tflops, burst)",
+                "flops_per_step": w.flops(), "traffic": None}
+    traffic_file = os.path.join(REPO, "profiles", f"traffic_{args.workload}.json")
+    if os.path.exists(traffic_file):
+        try:
+            roof["traffic"] = json.load(open(traffic_file)).get("dram_bytes_per_step")
+        except Exception:
+            pass
+
+    line = {"metric": "decode tokens/s" if isinstance(w, DecodeWorkload) else "attn tokens/s",
+            "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16" if isinstance(w, DecodeWorkload) else str(w.dt).split(".")[-1],
+            "data": "synthetic (seeded N(0,1); no dataset or checkpoint)",
+            "config": dict({"workload": WORKLOADS[args.workload], "parallelism": f"shard{world} (sequences per rank)"},
+                           **(w.config() if isinstance(w, DecodeWorkload) else {})),
+            "roofline": roof,
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": w.kernel_launches_per_step() * args.steps,
+            "clocks": clocks}
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tps, threads, secs, steps = cpu_decode_sample(16, max_seconds=12.0)
+        line["cpu_baseline"] = {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                                "sample": f"16 of 256 sequences of the c5 workload, {steps} step(s) in {secs:.1f} s; "
+                                          "C restatement of the reference's Java CPU attention (no JDK here)"}
+    if rank == 0 and world == 1 and not args.no_suite:
+        line["suite"] = run_suite(ctx, hbm, tflops, src)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

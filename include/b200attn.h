@@ -1,0 +1,251 @@
+/*
+ * b200attn.h -- C ABI of libb200attn.so, the B200 (sm_100a) backend for the
+ * attention hot path of win-directml-java: RoPE + scaled-dot-product attention
+ * for causal GQA prefill, single-token decode over a KV cache, and masked
+ * bidirectional encoder attention.
+ *
+ * Conventions
+ *   - Plain C.  Every entry point returns an int status (b2a_status); no
+ *     exception or C++ type crosses the boundary.  On failure the message is
+ *     kept per context and read with b2a_last_error().
+ *   - Tensor pointers are caller-owned DEVICE pointers unless a parameter
+ *     says "host".  `stream` is a cudaStream_t passed as void* (NULL = the
+ *     legacy default stream).  Calls are asynchronous on that stream.
+ *   - A context is bound to one CUDA device.  It is not thread-safe: use one
+ *     context per thread, as the reference's kernels are used per thread.
+ *   - There is no CPU fallback: a call that cannot run on the GPU fails.
+ *   - Element types follow the reference's TensorDataType names.
+ *
+ * Reference paths below are relative to the win-directml-java project:
+ *   WB/  = directml-windows-bindings/src/main/java/com/aresstack/windirectml/
+ *   INF/ = directml-inference/src/main/java/com/aresstack/windirectml/inference/
+ *   ENC/ = directml-encoder/src/main/java/com/aresstack/windirectml/encoder/
+ */
+#ifndef B200ATTN_H
+#define B200ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define B2A_API __attribute__((visibility("default")))
+#else
+#define B2A_API
+#endif
+
+#define B2A_ABI_VERSION 1
+
+typedef struct b2a_context b2a_context;
+
+/* Status codes.  The reference wraps native failures in the unchecked
+ * DirectMlRuntimeException (WB/runtime/DirectMlRuntimeException.java) and
+ * rejects bad shapes with IllegalArgumentException; a binding maps every
+ * non-zero status to one of those with b2a_last_error() as the message. */
+typedef enum b2a_status {
+    B2A_OK = 0,
+    B2A_EINVAL = 1,   /* bad shape, dtype, head divisibility, null or misaligned pointer */
+    B2A_ECUDA = 2,    /* a CUDA runtime call failed */
+    B2A_ENCCL = 3,    /* reserved for collective failures */
+    B2A_ETIMEOUT = 4, /* a bounded device-side wait ran out */
+    B2A_EOOM = 5,     /* device allocation failed or exceeded the context's cap */
+    B2A_ENOTSUP = 6,  /* valid arguments, but no kernel for this combination */
+    B2A_EDEVICE = 7   /* a device-side argument check failed (see b2a_check_device_status) */
+} b2a_status;
+
+/* TensorDataType FLOAT32 / FLOAT16 / BFLOAT16 (WB/runtime/TensorDataType.java). */
+typedef enum b2a_dtype {
+    B2A_FLOAT32 = 0,
+    B2A_FLOAT16 = 1,
+    B2A_BFLOAT16 = 2
+} b2a_dtype;
+
+/* Activation layouts.
+ * HEAD_MAJOR = [B, H, S, D] (AttentionKernel contract, WB/runtime/kernels/AttentionKernel.java:11-13).
+ * SEQ_MAJOR  = [B, S, H, D] (the encoders' flat [seq][H*D] rows,
+ *              ENC/minilm/CpuMiniLmEncoder.java:311-316). */
+typedef enum b2a_layout {
+    B2A_HEAD_MAJOR = 0,
+    B2A_SEQ_MAJOR = 1
+} b2a_layout;
+
+/* KV cache layouts, per sequence.
+ * KV_HEAD_MAJOR = [B][Hkv][max_seq][D] (INF/decoderonly/DecoderOnlyKvCacheLayout.java:53-59,
+ *                 WB/windows/QwenAttentionShaders.java:73-75).
+ * KV_POS_MAJOR  = [B][max_seq][Hkv][D] (INF/decoderonly/DecoderOnlyWarpLayerKvCache.java:13-45,
+ *                 INF/gemma/Gemma3WarpFusedAttentionContextKernel.java:58). */
+typedef enum b2a_kv_layout {
+    B2A_KV_HEAD_MAJOR = 0,
+    B2A_KV_POS_MAJOR = 1
+} b2a_kv_layout;
+
+/* Rotary embedding variants.  Both rotate the pairs (x[i], x[i+D/2]) by
+ * angle = pos * theta^(-2i/D), the angle taken in double precision.
+ * NEOX    : DecoderOnlyRotaryEmbedding (INF/decoderonly/DecoderOnlyRotaryEmbedding.java:42-67),
+ *           cos/sin rounded to float, rotation in float.
+ * GEMMA   : Gemma3ReferenceMath.applyRopeHalf (INF/gemma/Gemma3ReferenceMath.java:65-83),
+ *           rotation in double, result rounded to float. */
+typedef enum b2a_rope_mode {
+    B2A_ROPE_NONE = 0,
+    B2A_ROPE_NEOX = 1,
+    B2A_ROPE_GEMMA = 2
+} b2a_rope_mode;
+
+/* ---------------------------------------------------------------- lifecycle */
+
+/* Create a context on CUDA device `device` (replaces DirectMlContextImpl
+ * initialisation, WB/runtime/DirectMlContextImpl.java). */
+B2A_API int b2a_create(int device, b2a_context** out);
+
+/* Destroy the context and free its workspace (AutoCloseable.close of the
+ * reference kernels, WB/runtime/kernels/DirectMlAttentionKernel.java:592-617). */
+B2A_API int b2a_destroy(b2a_context* ctx);
+
+/* Copy the last error message of `ctx` into buf (NUL-terminated, truncated
+ * to n bytes).  Returns the full message length.  ctx may be NULL for errors
+ * of b2a_create. */
+B2A_API int b2a_last_error(const b2a_context* ctx, char* buf, size_t n);
+
+/* Static name of a status code. */
+B2A_API const char* b2a_status_string(int status);
+
+/* ABI version (B2A_ABI_VERSION) and build string. */
+B2A_API int b2a_abi_version(void);
+B2A_API const char* b2a_build_info(void);
+
+/* Cap on the bytes of device workspace the context may allocate (0 = no
+ * cap).  A call whose workspace would exceed it fails with B2A_EOOM. */
+B2A_API int b2a_set_workspace_limit(b2a_context* ctx, size_t bytes);
+
+/* Bytes of device workspace the context currently holds. */
+B2A_API int b2a_workspace_bytes(const b2a_context* ctx, size_t* bytes);
+
+/* Pre-allocate the decode workspace for batches up to max_batch with the
+ * given head geometry, so later b2a_decode calls allocate nothing. */
+B2A_API int b2a_reserve_decode(b2a_context* ctx, int max_batch, int num_q_heads, int num_kv_heads,
+                               int head_dim);
+
+/* Synchronise `stream` and report device-side argument checks raised since
+ * the last call (for example a ctx_lens entry outside [0, max_seq)).
+ * Returns B2A_OK or B2A_EDEVICE and clears the flag. */
+B2A_API int b2a_check_device_status(b2a_context* ctx, void* stream);
+
+/* ------------------------------------------------------------ encoder MHA */
+
+/* Multi-head scaled-dot-product attention, bidirectional, with an optional key
+ * padding mask: the AttentionKernel.dispatch(q, k, v, mask, y, scale) contract
+ * (WB/runtime/kernels/AttentionKernel.java:19-24; validation as
+ * DirectMlAttentionKernel.recordOnto, WB/runtime/kernels/DirectMlAttentionKernel.java:401-420,663-685).
+ *   q, k, v, y : [B,H,S,D] (HEAD_MAJOR) or [B,S,H,D] (SEQ_MAJOR), element type in_dtype for
+ *                q/k/v and out_dtype for y.
+ *   mask       : optional additive float mask [B,S] (0 or -1e9, the [B,1,1,S] tensor of
+ *                BertPoolingWeights.additiveMask, ENC/bert/BertPoolingWeights.java:62-77), or NULL.
+ *   key_lengths: optional int32 [B]; key j of batch b is masked iff j >= key_lengths[b]
+ *                (the CPU encoders' int attention mask, ENC/minilm/CpuMiniLmEncoder.java:337).
+ *                At most one of mask / key_lengths may be non-NULL.
+ *   scale      : usually 1/sqrt(D).
+ * A masked key contributes exactly zero weight; a row whose keys are all masked
+ * yields the mean of V, as softmax over equal -1e9 scores does in the reference. */
+B2A_API int b2a_mha(b2a_context* ctx, int in_dtype, int out_dtype,
+                    const void* q, const void* k, const void* v,
+                    const float* mask, const int32_t* key_lengths, void* y,
+                    int B, int H, int S, int D, float scale, int layout, void* stream);
+
+/* ------------------------------------------------------------ causal prefill */
+
+/* Causal grouped-query attention over a whole prompt with RoPE fused
+ * (SmolLM2ReferenceForwardPass.runSelfAttention, INF/smollm2/SmolLM2ReferenceForwardPass.java:167-210;
+ *  Qwen2Runtime.processLayerPrefill attention, INF/qwen/Qwen2Runtime.java:916-971;
+ *  Phi3Runtime prefill attention, INF/phi3/Phi3Runtime.java:609-697).
+ *   q : [B,S,Hq,D], k/v : [B,S,Hkv,D] (in_dtype), o : [B,S,Hq,D] (out_dtype); Hq % Hkv == 0,
+ *       query head h reads kv head h / (Hq/Hkv) (INF/decoderonly/DecoderOnlyAttentionLayout.java:43-53).
+ *   rope_mode / rope_theta : rotation applied to q and k at positions pos0 + s
+ *       (B2A_ROPE_NONE to skip).  q, k, v are not modified.
+ *   window : 0 = full causal; > 0 = keys [max(0, t-window+1), t]
+ *       (INF/gemma/Gemma3AttentionLayout.java:57-62).
+ *   k_rot_out : optional [B,S,Hkv,D] (in_dtype) receiving the rotated keys (the KV-cache
+ *       store of Qwen2Runtime.java:927-936), or NULL.  For f16/bf16 inputs on the
+ *       tensor-core path it doubles as the rotated-key staging buffer; pass NULL to
+ *       let the context hold that buffer. */
+B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype,
+                               const void* q, const void* k, const void* v, void* o,
+                               int B, int S, int Hq, int Hkv, int D, float scale,
+                               int rope_mode, double rope_theta, int pos0, int window,
+                               void* k_rot_out, void* stream);
+
+/* ------------------------------------------------------------ decode */
+
+/* One decode step for a batch of sequences, fused: optional per-head QK-norm
+ * (zero-centred RMSNorm x*rsqrt(mean(x^2)+eps)*(1+w), INF/gemma/Gemma3ReferenceMath.java:25-46),
+ * RoPE of the new q and k at position ctx_lens[b], append of k and v into the
+ * cache at that position, then attention of every q head over the visible
+ * keys [first, ctx_lens[b]] including the new one, first = 0 or
+ * max(0, ctx_lens[b]-window+1).  Mirrors Qwen2Runtime.processLayerDecode
+ * (INF/qwen/Qwen2Runtime.java:723-766), the Qwen GPU pair rope_and_append +
+ * gqa_attention_decode (WB/windows/QwenAttentionShaders.java:82-263) and the
+ * Gemma decode step (INF/gemma/Gemma3WarpLayer.java:263-281,
+ * INF/gemma/Gemma3ReferenceForwardPass.java:124-182).
+ *   q_new [B,Hq,D], k_new / v_new [B,Hkv,D] : element type q_dtype.
+ *   k_cache / v_cache : cache_dtype, layout kv_layout, capacity max_seq positions.
+ *   ctx_lens : DEVICE int32 [B], tokens already cached per sequence (the new
+ *              token's position); each must lie in [0, max_seq).  Entries
+ *              outside raise the device status (b2a_check_device_status) and that
+ *              sequence's output is NaN.
+ *   q_norm_w / k_norm_w : optional DEVICE float [D] QK-norm weights (both or neither).
+ *   o [B,Hq,D] : out_dtype. */
+B2A_API int b2a_decode(b2a_context* ctx, int q_dtype, int cache_dtype, int out_dtype,
+                       const void* q_new, const void* k_new, const void* v_new,
+                       void* k_cache, void* v_cache, int kv_layout, const int32_t* ctx_lens,
+                       int B, int Hq, int Hkv, int D, int max_seq, float scale,
+                       int rope_mode, double rope_theta, int window,
+                       const float* q_norm_w, const float* k_norm_w, float norm_eps,
+                       void* o, void* stream);
+
+/* ------------------------------------------- reference GPU contracts, 1:1 */
+
+/* ROPE_AND_APPEND_HLSL (WB/windows/QwenAttentionShaders.java:82-135), root
+ * constants {numHeads, kvHeads, headDim, pos, maxSeqLen, ropeTheta}: rotates
+ * q [numHeads*headDim] in place and writes the rotated k and the unchanged v
+ * [kvHeads*headDim] into the float caches [kvHeads][maxSeqLen][headDim] at
+ * position pos.  All float32.  The angle is taken in double precision. */
+B2A_API int b2a_qwen_rope_and_append(b2a_context* ctx, float* q, const float* k, const float* v,
+                                     float* k_cache, float* v_cache, int num_heads, int kv_heads,
+                                     int head_dim, int pos, int max_seq_len, float rope_theta,
+                                     void* stream);
+
+/* GQA_ATTENTION_DECODE_HLSL (WB/windows/QwenAttentionShaders.java:168-263), root
+ * constants {numHeads, kvHeads, headDim, qHeadsPerKvHead, seqLen, maxSeqLen, scale}:
+ * attn_out[h] = softmax(scale * q[h].K[0..seqLen)) . V over the float caches
+ * [kvHeads][maxSeqLen][headDim], kv head h / qHeadsPerKvHead. */
+B2A_API int b2a_qwen_gqa_attention_decode(b2a_context* ctx, const float* q, const float* k_cache,
+                                          const float* v_cache, float* attn_out, int num_heads,
+                                          int kv_heads, int head_dim, int q_heads_per_kv_head,
+                                          int seq_len, int max_seq_len, float scale, void* stream);
+
+/* FUSED_ATTENTION_HLSL (INF/gemma/Gemma3WarpFusedAttentionContextKernel.java:32-86,
+ * call contract L111-135), constants {numHeads, groupsPerKv, headDim, kvDim,
+ * firstValid, queryPos, scale}: ctx_out[h] = softmax over keys
+ * [firstValid, queryPos] of the position-major float caches keys/values
+ * [pos][kvDim], kv head h / groupsPerKv.  head_dim <= 256. */
+B2A_API int b2a_gemma_fused_attention_context(b2a_context* ctx, const float* q, const float* keys,
+                                              const float* values, float* ctx_out, int num_heads,
+                                              int groups_per_kv, int head_dim, int kv_dim,
+                                              int first_valid, int query_pos, float scale, void* stream);
+
+/* ------------------------------------------------------------ multi-GPU */
+
+/* Partition `n_units` independent (sequence, kv-head) units over `n_ranks`
+ * ranks with equal unit counts (n_units % n_ranks == 0 required), balancing
+ * the per-unit cost `unit_cost` (host, e.g. KV bytes) by a longest-first
+ * greedy assignment.  Writes rank_of_unit[n_units] (host).  No collective is
+ * involved; outputs are reassembled by the caller (an all-gather). */
+B2A_API int b2a_partition_units(int n_units, int n_ranks, const int64_t* unit_cost, int32_t* rank_of_unit);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200ATTN_H */

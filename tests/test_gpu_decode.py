@@ -1,0 +1,148 @@
+"""Decode parity: the CUDA decode step through the C ABI against the oracle.
+
+Each case draws seeded inputs rounded to the cache dtype, runs
+``b2a_decode`` (fused QK-norm + RoPE + KV append + split-KV attention) and
+compares the output with ``oracle.decode`` (max abs <= 2e-3, cosine >=
+0.9999) and the appended cache rows with the oracle's (one ulp of the cache
+type); every other cache row must be untouched (bit-exact).
+"""
+import numpy as np
+import pytest
+
+import oracle
+from helpers import assert_close, normal, to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _run_case(ctx, *, B, Hq, Hkv, D, max_seq, lens, cache_dtype=oracle.F16, q_dtype=oracle.F16,
+              layout=oracle.KV_HEAD_MAJOR, rope_mode="neox", theta=1e6, window=0, qk_norm=False, seed=11,
+              out_dtype=oracle.F32):
+    import torch
+    import b200attn
+    lens = np.asarray(lens, np.int32)
+    q = normal(seed, (B, Hq, D), q_dtype)
+    kn = normal(seed + 1, (B, Hkv, D), q_dtype)
+    vn = normal(seed + 2, (B, Hkv, D), q_dtype)
+    shape = (B, Hkv, max_seq, D) if layout == oracle.KV_HEAD_MAJOR else (B, max_seq, Hkv, D)
+    kc = normal(seed + 3, shape, cache_dtype)
+    vc = normal(seed + 4, shape, cache_dtype)
+    qw = kw = None
+    if qk_norm:
+        qw = (0.5 * normal(seed + 5, (D,), oracle.F32)).astype(np.float32)
+        kw = (0.5 * normal(seed + 6, (D,), oracle.F32)).astype(np.float32)
+    scale = float(np.float32(1.0 / np.sqrt(D)))
+    orc_rope = oracle.ROPE_GEMMA if rope_mode == "gemma" else oracle.ROPE_DECODERONLY
+    want, kc_want, vc_want = oracle.decode(
+        q, kn, vn, kc, vc, lens, B=B, Hq=Hq, Hkv=Hkv, D=D, max_seq=max_seq, scale=scale,
+        rope_theta=theta if rope_mode else 0.0, rope_mode=orc_rope, window=window, cache_layout=layout,
+        cache_dtype=cache_dtype, q_norm_w=qw, k_norm_w=kw, norm_eps=1e-6,
+        softmax_mode=oracle.SOFTMAX_GEMMA if rope_mode == "gemma" else oracle.SOFTMAX_DECODERONLY)
+
+    kc_d, vc_d = to_dev(kc, cache_dtype), to_dev(vc, cache_dtype)
+    out = torch.empty((B, Hq, D), dtype={oracle.F32: torch.float32, oracle.F16: torch.float16,
+                                          oracle.BF16: torch.bfloat16}[out_dtype], device="cuda")
+    b_rope = {None: b200attn.ROPE_NONE, "neox": b200attn.ROPE_NEOX, "gemma": b200attn.ROPE_GEMMA}[rope_mode]
+    b200attn.decode(ctx, to_dev(q, q_dtype), to_dev(kn, q_dtype), to_dev(vn, q_dtype), kc_d, vc_d,
+                    torch.from_numpy(lens).cuda(), out, scale,
+                    kv_layout=b200attn.KV_HEAD_MAJOR if layout == oracle.KV_HEAD_MAJOR else b200attn.KV_POS_MAJOR,
+                    rope_mode=b_rope, rope_theta=theta, window=window,
+                    q_norm_w=None if qw is None else torch.from_numpy(qw).cuda(),
+                    k_norm_w=None if kw is None else torch.from_numpy(kw).cuda(), norm_eps=1e-6)
+    ctx.check_device_status()
+    got = to_np(out)
+    err, cos = assert_close(got, want, what="decode output")
+    # appended rows: within one ulp of the cache type; everything else untouched
+    kc_got, vc_got = to_np(kc_d), to_np(vc_d)
+    ulp = {oracle.F16: 2 ** -10, oracle.BF16: 2 ** -7, oracle.F32: 2 ** -23}[cache_dtype]
+    np.testing.assert_allclose(kc_got, kc_want, rtol=ulp, atol=1e-6)
+    np.testing.assert_array_equal(vc_got, vc_want)
+    return err, cos
+
+
+def test_decode_qwen_shape_head_major(ctx):
+    # configs[2] geometry (14/2 heads, D=64, theta 1e6) at a small batch
+    lens = [0, 1, 63, 64, 65, 600, 699, 317]
+    _run_case(ctx, B=8, Hq=14, Hkv=2, D=64, max_seq=700, lens=lens, theta=1e6)
+
+
+def test_decode_qwen_shape_bf16_cache(ctx):
+    _run_case(ctx, B=5, Hq=14, Hkv=2, D=64, max_seq=300, lens=[5, 128, 299, 0, 77], cache_dtype=oracle.BF16,
+              q_dtype=oracle.BF16, seed=21)
+
+
+@pytest.mark.parametrize("window,theta", [(512, 1e4), (0, 1e6)])
+def test_decode_gemma_shape_local_and_global(ctx, window, theta):
+    # configs[4] geometry: 4/1 heads, D=256, QK-norm, Gemma RoPE, position-major cache
+    lens = [0, 511, 512, 513, 1500, 1999]
+    _run_case(ctx, B=6, Hq=4, Hkv=1, D=256, max_seq=2000, lens=lens, layout=oracle.KV_POS_MAJOR,
+              rope_mode="gemma", theta=theta, window=window, qk_norm=True, seed=31)
+
+
+def test_decode_pos_major_multi_kv_head(ctx):
+    _run_case(ctx, B=3, Hq=8, Hkv=2, D=128, max_seq=400, lens=[10, 399, 200], layout=oracle.KV_POS_MAJOR, seed=41)
+
+
+def test_decode_more_than_eight_heads_per_kv_head(ctx):
+    _run_case(ctx, B=2, Hq=16, Hkv=1, D=128, max_seq=300, lens=[150, 299], seed=51)
+
+
+def test_decode_mha_head_dim_96(ctx):
+    _run_case(ctx, B=3, Hq=4, Hkv=4, D=96, max_seq=260, lens=[0, 100, 259], seed=61)
+
+
+def test_decode_long_sequence_splits_and_merges(ctx):
+    # few sequences with long contexts force many chunks per sequence and the log-sum-exp merge
+    _run_case(ctx, B=2, Hq=7, Hkv=1, D=64, max_seq=40000, lens=[39999, 3], seed=71)
+
+
+def test_decode_no_rope(ctx):
+    _run_case(ctx, B=2, Hq=4, Hkv=2, D=64, max_seq=100, lens=[50, 99], rope_mode=None, seed=81)
+
+
+def test_decode_fp16_output(ctx):
+    _run_case(ctx, B=4, Hq=14, Hkv=2, D=64, max_seq=500, lens=[1, 2, 400, 499], out_dtype=oracle.F16, seed=91)
+
+
+def test_decode_generic_kernel_float32_cache(ctx):
+    # float32 caches and head_dim 8 take the generic warp-per-head kernel
+    _run_case(ctx, B=3, Hq=2, Hkv=1, D=8, max_seq=40, lens=[0, 17, 39], cache_dtype=oracle.F32,
+              q_dtype=oracle.F32, theta=1e4, seed=101)
+
+
+def test_decode_generic_kernel_odd_head_dim(ctx):
+    _run_case(ctx, B=2, Hq=6, Hkv=3, D=48, max_seq=90, lens=[33, 89], seed=111)
+
+
+def test_decode_rejects_out_of_range_ctx_len(ctx):
+    import torch
+    import b200attn
+    B, Hq, Hkv, D, S = 2, 2, 1, 64, 16
+    z = lambda *s: torch.zeros(*s, dtype=torch.float16, device="cuda")
+    out = torch.zeros(B, Hq, D, device="cuda")
+    lens = torch.tensor([3, 16], dtype=torch.int32, device="cuda")  # 16 == max_seq: invalid
+    b200attn.decode(ctx, z(B, Hq, D), z(B, Hkv, D), z(B, Hkv, D), z(B, Hkv, S, D), z(B, Hkv, S, D), lens, out,
+                    0.125)
+    with pytest.raises(b200attn.B200RuntimeException, match="B2A_EDEVICE"):
+        ctx.check_device_status()
+    o = out.cpu().numpy()
+    assert np.all(np.isnan(o[1])) and np.all(np.isfinite(o[0]))
+
+
+def test_decode_argument_validation(ctx):
+    import torch
+    import b200attn
+    z = lambda *s: torch.zeros(*s, dtype=torch.float16, device="cuda")
+    lens = torch.zeros(1, dtype=torch.int32, device="cuda")
+    with pytest.raises(ValueError, match="divisible"):
+        b200attn.decode(ctx, z(1, 14, 64), z(1, 3, 64), z(1, 3, 64), z(1, 3, 8, 64), z(1, 3, 8, 64), lens,
+                        torch.zeros(1, 14, 64, device="cuda"), 0.125)
+    with pytest.raises(ValueError, match="together"):
+        b200attn.decode(ctx, z(1, 2, 64), z(1, 1, 64), z(1, 1, 64), z(1, 1, 8, 64), z(1, 1, 8, 64), lens,
+                        torch.zeros(1, 2, 64, device="cuda"), 0.125, q_norm_w=torch.ones(64, device="cuda"))
+
+
+def test_decode_full_size_qwen_config(ctx):
+    """configs[2] at full size: B=64, 14/2, D=64, fp16 cache, ctx ~ U[512, 8192]."""
+    lens = oracle.splitmix_uniform_int(3, 64, 512, 8192)
+    _run_case(ctx, B=64, Hq=14, Hkv=2, D=64, max_seq=8193, lens=lens, theta=1e6, seed=3000)

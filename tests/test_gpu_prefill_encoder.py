@@ -1,0 +1,153 @@
+"""Prefill and encoder parity through the C ABI against the oracle."""
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+from helpers import assert_close, normal, to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+
+TORCH = {oracle.F32: "float32", oracle.F16: "float16", oracle.BF16: "bfloat16"}
+
+
+def _prefill_case(ctx, *, B, S, Hq, Hkv, D, dtype, out_dtype, theta, window=0, pos0=0, seed=1, rope=True):
+    import torch
+    import b200attn
+    q = normal(seed, (B, S, Hq, D), dtype)
+    k = normal(seed + 1, (B, S, Hkv, D), dtype)
+    v = normal(seed + 2, (B, S, Hkv, D), dtype)
+    scale = float(np.float32(1.0 / math.sqrt(D)))
+    want = oracle.prefill(q, k, v, B=B, S=S, Hq=Hq, Hkv=Hkv, D=D, scale=scale, rope_theta=theta if rope else 0.0,
+                          pos0=pos0, window=window)
+    o = torch.empty((B, S, Hq, D), dtype=getattr(torch, TORCH[out_dtype]), device="cuda")
+    b200attn.prefill_causal(ctx, to_dev(q, dtype), to_dev(k, dtype), to_dev(v, dtype), o, scale,
+                            rope_mode=b200attn.ROPE_NEOX if rope else b200attn.ROPE_NONE, rope_theta=theta, pos0=pos0,
+                            window=window)
+    torch.cuda.synchronize()
+    return to_np(o), want
+
+
+def test_prefill_smollm2_config_fp32(ctx):
+    """configs[0] exactly: B=1, S=256, 9/3 heads, D=64, NeoX RoPE theta 1e5, fp32 in/out."""
+    got, want = _prefill_case(ctx, B=1, S=256, Hq=9, Hkv=3, D=64, dtype=oracle.F32, out_dtype=oracle.F32,
+                              theta=1e5, seed=1)
+    err, _ = assert_close(got, want, atol=2e-3, what="smollm2 prefill")
+    assert err < 1e-4  # fp32 end to end
+
+
+def test_prefill_phi3_shape_bf16(ctx):
+    """configs[3] geometry (32 heads MHA, D=96, theta 1e4, bf16) at a reduced size."""
+    got, want = _prefill_case(ctx, B=1, S=384, Hq=4, Hkv=4, D=96, dtype=oracle.BF16, out_dtype=oracle.F32,
+                              theta=1e4, seed=5)
+    assert_close(got, want, what="phi3-shaped prefill (fp32 out)")
+
+
+def test_prefill_bf16_output_within_tolerance_plus_rounding(ctx):
+    """A bf16 output cannot meet 2e-3 where |o| >= 0.5 (one ulp is 3.9e-3 there), so the bar is
+    2e-3 plus half a bf16 ulp of the oracle value: the compute tolerance plus the output rounding."""
+    got, want = _prefill_case(ctx, B=1, S=200, Hq=2, Hkv=2, D=96, dtype=oracle.BF16, out_dtype=oracle.BF16,
+                              theta=1e4, seed=7)
+    half_ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(want), 2.0 ** -126))) - 8)
+    assert np.all(np.abs(got - want) <= 2e-3 + half_ulp)
+
+
+@pytest.mark.parametrize("D", [32, 64, 128])
+def test_prefill_fp16_gqa_window(ctx, D):
+    got, want = _prefill_case(ctx, B=2, S=200, Hq=8, Hkv=2, D=D, dtype=oracle.F16, out_dtype=oracle.F32,
+                              theta=1e4, window=50, seed=9 + D)
+    assert_close(got, want, what=f"fp16 windowed prefill D={D}")
+
+
+def test_prefill_position_offset_and_no_rope(ctx):
+    got, want = _prefill_case(ctx, B=1, S=70, Hq=4, Hkv=1, D=64, dtype=oracle.F16, out_dtype=oracle.F32, theta=1e6,
+                              pos0=1000, seed=13)
+    assert_close(got, want, what="pos0 offset")
+    got, want = _prefill_case(ctx, B=1, S=70, Hq=4, Hkv=1, D=64, dtype=oracle.F16, out_dtype=oracle.F32, theta=0,
+                              rope=False, seed=14)
+    assert_close(got, want, what="no rope")
+
+
+def test_prefill_generic_path_head_dim_40(ctx):
+    got, want = _prefill_case(ctx, B=1, S=90, Hq=3, Hkv=1, D=40, dtype=oracle.F16, out_dtype=oracle.F32, theta=1e4,
+                              seed=15)
+    assert_close(got, want, what="generic D=40")
+
+
+# ------------------------------------------------------------------ encoder
+def _encoder_case(ctx, *, B, H, S, D, dtype, lens, layout, seed):
+    import torch
+    import b200attn
+    shape = (B, H, S, D) if layout == 0 else (B, S, H, D)
+    q, k, v = (normal(seed + i, shape, dtype) for i in range(3))
+    want = oracle.encoder_minilm(q, k, v, lens, B=B, H=H, S=S, D=D, layout=layout)
+    y = torch.empty(shape, dtype=torch.float32, device="cuda")
+    b200attn.mha(ctx, to_dev(q, dtype), to_dev(k, dtype), to_dev(v, dtype), y, 1.0 / math.sqrt(D),
+                 key_lengths=torch.from_numpy(np.asarray(lens, np.int32)).cuda(),
+                 layout=b200attn.HEAD_MAJOR if layout == 0 else b200attn.SEQ_MAJOR)
+    torch.cuda.synchronize()
+    return to_np(y), want
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+def test_encoder_minilm_config_full_size(ctx, layout):
+    """configs[1] at full size: B=64, S=128, H=12, D=32, fp16, key lengths ~ U[16,128]."""
+    lens = oracle.splitmix_uniform_int(2, 64, 16, 128)
+    got, want = _encoder_case(ctx, B=64, H=12, S=128, D=32, dtype=oracle.F16, lens=lens, layout=layout, seed=200)
+    assert_close(got, want, what="minilm encoder")
+
+
+def test_encoder_zero_and_full_lengths(ctx):
+    # a text with no valid key averages V (softmax of equal -1e9 scores), as the reference does
+    got, want = _encoder_case(ctx, B=3, H=2, S=64, D=32, dtype=oracle.F16, lens=[0, 64, 1], layout=1, seed=300)
+    assert_close(got, want, what="edge lengths")
+
+
+def test_encoder_fp32_generic_odd_sequence(ctx):
+    got, want = _encoder_case(ctx, B=2, H=3, S=37, D=24, dtype=oracle.F32, lens=[37, 5], layout=0, seed=310)
+    assert_close(got, want, atol=1e-4, what="fp32 encoder")
+
+
+@pytest.mark.parametrize("with_mask", [False, True])
+def test_attention_kernel_contract_directml_cases(ctx, with_mask):
+    """DirectMlAttentionKernelTest (runtime/kernels/DirectMlAttentionKernelTest.java:39-127):
+    B=1,H=2,S=4,D=8 FLOAT32, Random(0xA77E47 / 0xDEC0DE) inputs, one blocked key per batch, tol 5e-4."""
+    import torch
+    import b200attn
+    B, H, S, D = 1, 2, 4, 8
+    scale = float(np.float32(1.0 / math.sqrt(D)))
+    rng = oracle.JavaRandom(0xA77E47 if with_mask else 0xDEC0DE)
+    q, k, v = (rng.floats_centered(B * H * S * D) for _ in range(3))
+    mask = None
+    if with_mask:
+        mask = np.zeros(B * S, np.float32)
+        for b in range(B):
+            mask[b * S + rng.next_int(S)] = np.float32(-1e9)
+    want = oracle.mha_additive(q, k, v, mask, B=B, H=H, S=S, D=D, scale=scale)
+    kern = b200attn.CudaAttentionKernel(ctx, B, H, S, D, scale, with_mask)
+    dev = lambda a: torch.from_numpy(a).cuda()
+    y = torch.empty(B * H * S * D, device="cuda")
+    kern.dispatch(dev(q), dev(k), dev(v), None if mask is None else dev(mask), y, scale)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(y.cpu().numpy(), want, atol=5e-4)
+    with pytest.raises(b200attn.B200RuntimeException, match="scale mismatch"):
+        kern.dispatch(dev(q), dev(k), dev(v), None, y, scale * 2)
+
+
+def test_encoder_additive_mask_fp16(ctx):
+    import torch
+    import b200attn
+    B, H, S, D = 4, 3, 96, 64
+    lens = [96, 40, 1, 70]
+    q, k, v = (normal(400 + i, (B, H, S, D), oracle.F16) for i in range(3))
+    mask = np.zeros((B, S), np.float32)
+    for b, L in enumerate(lens):
+        mask[b, L:] = -1e9
+    scale = float(np.float32(1.0 / math.sqrt(D)))
+    want = oracle.mha_additive(q, k, v, mask, B=B, H=H, S=S, D=D, scale=scale)
+    y = torch.empty((B, H, S, D), device="cuda")
+    b200attn.mha(ctx, to_dev(q, oracle.F16), to_dev(k, oracle.F16), to_dev(v, oracle.F16), y, scale,
+                 mask=torch.from_numpy(mask).cuda())
+    torch.cuda.synchronize()
+    assert_close(to_np(y), want, what="additive mask")

@@ -1,0 +1,659 @@
+// api.cpp -- the C ABI of libb200attn.so (include/b200attn.h): contexts,
+// argument validation with the reference's error wording, workspace
+// management and kernel dispatch.  No exception crosses the boundary and no
+// call falls back to the CPU.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <numeric>
+#include <string>
+#include <vector>
+
+#include "../../include/b200attn.h"
+#include "internal.h"
+
+using namespace b2a;
+
+struct b2a_context {
+    int device = 0;
+    int sm_count = 0;
+    std::string last_error;
+    size_t ws_limit = 0;  // 0: unlimited
+    int* status = nullptr;  // device int[4]
+    // decode workspace: [counters][partials]
+    void* dec_ws = nullptr;
+    size_t dec_ws_bytes = 0;
+    size_t dec_counter_ints = 0;
+    // prefill workspace: rope table + rotated q/k staging
+    void* pf_ws = nullptr;
+    size_t pf_ws_bytes = 0;
+};
+
+namespace {
+
+thread_local std::string g_create_error;
+
+int fail(b2a_context* ctx, int status, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    if (ctx) ctx->last_error = buf;
+    else g_create_error = buf;
+    return status;
+}
+
+int cuda_fail(b2a_context* ctx, cudaError_t e, const char* what) {
+    if (e == cudaErrorMemoryAllocation) return fail(ctx, B2A_EOOM, "%s: %s", what, cudaGetErrorString(e));
+    return fail(ctx, B2A_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+// Makes ctx->device current for the duration of a call.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+bool valid_dtype(int d) { return d == B2A_FLOAT32 || d == B2A_FLOAT16 || d == B2A_BFLOAT16; }
+size_t dtype_size(int d) { return d == B2A_FLOAT32 ? 4 : 2; }
+
+int ensure_buffer(b2a_context* ctx, void** buf, size_t* have, size_t need, const char* what) {
+    if (*have >= need) return B2A_OK;
+    const size_t other = (buf == &ctx->dec_ws ? ctx->pf_ws_bytes : ctx->dec_ws_bytes);
+    if (ctx->ws_limit != 0 && need + other > ctx->ws_limit)
+        return fail(ctx, B2A_EOOM, "%s workspace of %zu bytes exceeds the context limit of %zu bytes", what,
+                    need + other, ctx->ws_limit);
+    if (*buf) {
+        cudaFree(*buf);  // implicitly waits for work that may still use it
+        *buf = nullptr;
+        *have = 0;
+    }
+    cudaError_t e = cudaMalloc(buf, need);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_fail(ctx, e, what);
+    }
+    *have = need;
+    return B2A_OK;
+}
+
+void inv_freq_table(double theta, int D, double* out) {
+    // 1 / theta^(2i/D) in double (INF/decoderonly/DecoderOnlyRotaryEmbedding.java:57-59,
+    // INF/gemma/Gemma3ReferenceMath.java:74)
+    for (int i = 0; i < D / 2; ++i) out[i] = 1.0 / pow(theta, (2.0 * i) / D);
+}
+
+int check_heads(b2a_context* ctx, int Hq, int Hkv) {
+    // DecoderOnlyAttentionLayout constructor (INF/decoderonly/DecoderOnlyAttentionLayout.java:12-22)
+    if (Hq <= 0) return fail(ctx, B2A_EINVAL, "numQueryHeads must be positive");
+    if (Hkv <= 0) return fail(ctx, B2A_EINVAL, "numKeyValueHeads must be positive");
+    if (Hq % Hkv != 0)
+        return fail(ctx, B2A_EINVAL, "numQueryHeads must be divisible by numKeyValueHeads for grouped-query attention");
+    return B2A_OK;
+}
+
+int check_head_dim(b2a_context* ctx, int D) {
+    // DecoderOnlyRotaryEmbedding constructor (INF/decoderonly/DecoderOnlyRotaryEmbedding.java:14-16)
+    if (D <= 0 || D % 2 != 0) return fail(ctx, B2A_EINVAL, "headDim must be positive and even");
+    if (D > kMaxHeadDim) return fail(ctx, B2A_ENOTSUP, "headDim %d exceeds the supported maximum %d", D, kMaxHeadDim);
+    return B2A_OK;
+}
+
+int run_decode(b2a_context* ctx, DecodeParams& p, cudaStream_t stream, bool allow_tc) {
+    // 16-byte row loads need 16-byte aligned cache bases and row strides
+    const bool aligned = ((uintptr_t)p.k_cache % 16 == 0) && ((uintptr_t)p.v_cache % 16 == 0) &&
+                         p.stride_b % 8 == 0 && p.stride_h % 8 == 0 && p.stride_pos % 8 == 0;
+    p.status = ctx->status;
+    if (allow_tc && aligned && decode_tc_supported(p.D, p.cache_dtype)) {
+        p.n_hg = (p.G + 7) / 8;
+        int target = 0, cap = 0;
+        size_t partial_bytes = 0;
+        decode_tc_workspace(ctx->device, p.B, p.Hkv, p.n_hg, p.D, p.cache_dtype, &target, &cap, &partial_bytes);
+        const int bmax = std::min(p.B, kDecodeMaxBatchPerLaunch);
+        const size_t counter_ints = (size_t)bmax * p.Hkv * p.n_hg;
+        const size_t counter_bytes = (counter_ints * sizeof(int) + 255) / 256 * 256;
+        const size_t need = counter_bytes + partial_bytes;
+        const bool grow = need > ctx->dec_ws_bytes;
+        int rc = ensure_buffer(ctx, &ctx->dec_ws, &ctx->dec_ws_bytes, need, "decode");
+        if (rc != B2A_OK) return rc;
+        if (grow || counter_ints > ctx->dec_counter_ints) {
+            cudaError_t e = cudaMemsetAsync(ctx->dec_ws, 0, counter_bytes, stream);
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "decode workspace reset");
+            ctx->dec_counter_ints = counter_bytes / sizeof(int);
+        }
+        p.counters = static_cast<int*>(ctx->dec_ws);
+        p.partials = reinterpret_cast<float*>(static_cast<char*>(ctx->dec_ws) + counter_bytes);
+        p.target_items = target;
+        p.item_capacity = cap;
+        const int B = p.B;
+        // one launch covers at most kDecodeMaxBatchPerLaunch sequences and
+        // fewer than 2^31 visible keys (the kernel's int32 prefix)
+        const int per_launch = (int)std::min<int64_t>(kDecodeMaxBatchPerLaunch, INT32_MAX / ((int64_t)p.max_seq + 1));
+        for (int b0 = 0; b0 < B; b0 += per_launch) {
+            DecodeParams s = p;
+            s.B = std::min(per_launch, B - b0);
+            const size_t qe = dtype_size(p.q_dtype), oe = dtype_size(p.out_dtype), ce = dtype_size(p.cache_dtype);
+            s.q = static_cast<const char*>(p.q) + (size_t)b0 * p.Hq * p.D * qe;
+            if (p.k_new) s.k_new = static_cast<const char*>(p.k_new) + (size_t)b0 * p.Hkv * p.D * qe;
+            if (p.v_new) s.v_new = static_cast<const char*>(p.v_new) + (size_t)b0 * p.Hkv * p.D * qe;
+            s.k_cache = static_cast<char*>(p.k_cache) + (size_t)b0 * p.stride_b * ce;
+            s.v_cache = static_cast<char*>(p.v_cache) + (size_t)b0 * p.stride_b * ce;
+            if (p.ctx_lens) s.ctx_lens = p.ctx_lens + b0;
+            s.out = static_cast<char*>(p.out) + (size_t)b0 * p.Hq * p.D * oe;
+            cudaError_t e = launch_decode_tc(s, ctx->device, stream);
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "decode kernel launch");
+        }
+        return B2A_OK;
+    }
+    cudaError_t e = launch_decode_simt(p, stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "decode kernel launch");
+    return B2A_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+B2A_API const char* b2a_status_string(int status) {
+    switch (status) {
+        case B2A_OK: return "B2A_OK";
+        case B2A_EINVAL: return "B2A_EINVAL";
+        case B2A_ECUDA: return "B2A_ECUDA";
+        case B2A_ENCCL: return "B2A_ENCCL";
+        case B2A_ETIMEOUT: return "B2A_ETIMEOUT";
+        case B2A_EOOM: return "B2A_EOOM";
+        case B2A_ENOTSUP: return "B2A_ENOTSUP";
+        case B2A_EDEVICE: return "B2A_EDEVICE";
+        default: return "B2A_UNKNOWN";
+    }
+}
+
+B2A_API int b2a_abi_version(void) { return B2A_ABI_VERSION; }
+
+B2A_API const char* b2a_build_info(void) {
+    return "libb200attn sm_100a; CUDA " __DATE__ " " __TIME__;
+}
+
+B2A_API int b2a_create(int device, b2a_context** out) {
+    if (!out) return fail(nullptr, B2A_EINVAL, "out must not be null");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(nullptr, B2A_ECUDA, "no CUDA device available: %s", cudaGetErrorString(e));
+    }
+    if (device < 0 || device >= n) return fail(nullptr, B2A_EINVAL, "device %d out of range [0, %d)", device, n);
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return fail(nullptr, B2A_ECUDA, "cudaGetDeviceProperties: %s", cudaGetErrorString(e));
+    if (prop.major != 10 || prop.minor != 0)
+        return fail(nullptr, B2A_ENOTSUP, "device %d is sm_%d%d; this library is built for sm_100a (B200) only",
+                    device, prop.major, prop.minor);
+    DeviceGuard guard(device);
+    if (!guard.ok) return fail(nullptr, B2A_ECUDA, "cudaSetDevice(%d) failed", device);
+    b2a_context* ctx = new (std::nothrow) b2a_context();
+    if (!ctx) return fail(nullptr, B2A_EOOM, "host allocation failed");
+    ctx->device = device;
+    ctx->sm_count = prop.multiProcessorCount;
+    e = cudaMalloc(&ctx->status, 4 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ctx->status, 0, 4 * sizeof(int));
+    if (e != cudaSuccess) {
+        delete ctx;
+        return fail(nullptr, B2A_ECUDA, "status buffer: %s", cudaGetErrorString(e));
+    }
+    *out = ctx;
+    return B2A_OK;
+}
+
+B2A_API int b2a_destroy(b2a_context* ctx) {
+    if (!ctx) return B2A_OK;
+    {
+        DeviceGuard guard(ctx->device);
+        if (ctx->status) cudaFree(ctx->status);
+        if (ctx->dec_ws) cudaFree(ctx->dec_ws);
+        if (ctx->pf_ws) cudaFree(ctx->pf_ws);
+    }
+    delete ctx;
+    return B2A_OK;
+}
+
+B2A_API int b2a_last_error(const b2a_context* ctx, char* buf, size_t n) {
+    const std::string& s = ctx ? ctx->last_error : g_create_error;
+    if (buf && n > 0) {
+        size_t k = std::min(n - 1, s.size());
+        memcpy(buf, s.data(), k);
+        buf[k] = '\0';
+    }
+    return (int)s.size();
+}
+
+B2A_API int b2a_set_workspace_limit(b2a_context* ctx, size_t bytes) {
+    if (!ctx) return B2A_EINVAL;
+    ctx->ws_limit = bytes;
+    return B2A_OK;
+}
+
+B2A_API int b2a_workspace_bytes(const b2a_context* ctx, size_t* bytes) {
+    if (!ctx || !bytes) return B2A_EINVAL;
+    *bytes = ctx->dec_ws_bytes + ctx->pf_ws_bytes;
+    return B2A_OK;
+}
+
+B2A_API int b2a_reserve_decode(b2a_context* ctx, int max_batch, int num_q_heads, int num_kv_heads, int head_dim) {
+    if (!ctx) return B2A_EINVAL;
+    int rc = check_heads(ctx, num_q_heads, num_kv_heads);
+    if (rc) return rc;
+    if ((rc = check_head_dim(ctx, head_dim))) return rc;
+    if (max_batch <= 0) return fail(ctx, B2A_EINVAL, "max_batch must be positive");
+    if (!decode_tc_supported(head_dim, B2A_FLOAT16)) return B2A_OK;  // generic kernel needs no workspace
+    DeviceGuard guard(ctx->device);
+    const int n_hg = (num_q_heads / num_kv_heads + 7) / 8;
+    int target = 0, cap = 0;
+    size_t partial_bytes = 0;
+    decode_tc_workspace(ctx->device, max_batch, num_kv_heads, n_hg, head_dim, B2A_FLOAT16, &target, &cap,
+                        &partial_bytes);
+    const size_t counter_ints = (size_t)std::min(max_batch, kDecodeMaxBatchPerLaunch) * num_kv_heads * n_hg;
+    const size_t counter_bytes = (counter_ints * sizeof(int) + 255) / 256 * 256;
+    const bool grow = counter_bytes + partial_bytes > ctx->dec_ws_bytes;
+    rc = ensure_buffer(ctx, &ctx->dec_ws, &ctx->dec_ws_bytes, counter_bytes + partial_bytes, "decode");
+    if (rc) return rc;
+    if (grow || counter_ints > ctx->dec_counter_ints) {
+        cudaError_t e = cudaMemset(ctx->dec_ws, 0, counter_bytes);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "decode workspace reset");
+        ctx->dec_counter_ints = counter_bytes / sizeof(int);
+    }
+    return B2A_OK;
+}
+
+B2A_API int b2a_check_device_status(b2a_context* ctx, void* stream) {
+    if (!ctx) return B2A_EINVAL;
+    DeviceGuard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "stream synchronize");
+    int st[4] = {0, 0, 0, 0};
+    e = cudaMemcpy(st, ctx->status, sizeof(st), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "status read");
+    if (st[0] == 0) return B2A_OK;
+    cudaMemset(ctx->status, 0, sizeof(st));
+    std::string msg;
+    if (st[0] & 1) msg += "a ctx_lens entry was outside [0, max_seq); its outputs are NaN. ";
+    if (st[0] & 2) msg += "decode work items exceeded the workspace capacity. ";
+    if (st[0] & 4) msg += "a bf16 input exceeded the fp16 operand range (|x| > 65504). ";
+    return fail(ctx, B2A_EDEVICE, "%s", msg.c_str());
+}
+
+// ----------------------------------------------------------------- encoder
+B2A_API int b2a_mha(b2a_context* ctx, int in_dtype, int out_dtype, const void* q, const void* k, const void* v,
+                    const float* mask, const int32_t* key_lengths, void* y, int B, int H, int S, int D, float scale,
+                    int layout, void* stream) {
+    if (!ctx) return B2A_EINVAL;
+    if (!valid_dtype(in_dtype) || !valid_dtype(out_dtype))
+        return fail(ctx, B2A_EINVAL, "unsupported element type (in %d, out %d)", in_dtype, out_dtype);
+    if (!q || !k || !v || !y) return fail(ctx, B2A_EINVAL, "q, k, v and y tensors must not be null");
+    if (mask && key_lengths) return fail(ctx, B2A_EINVAL, "pass either an additive mask or key lengths, not both");
+    // DirectMlAttentionKernel constructor (WB/runtime/kernels/DirectMlAttentionKernel.java:109-111)
+    if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(ctx, B2A_EINVAL, "batch, heads, seq, headDim must be > 0");
+    if (D > kMaxHeadDim || D % 2) return fail(ctx, B2A_ENOTSUP, "headDim %d not supported (even, <= %d)", D, kMaxHeadDim);
+    if (layout != B2A_HEAD_MAJOR && layout != B2A_SEQ_MAJOR) return fail(ctx, B2A_EINVAL, "unknown layout %d", layout);
+    if (!(scale == scale) || scale <= 0.f) return fail(ctx, B2A_EINVAL, "scale must be a positive number");
+    DeviceGuard guard(ctx->device);
+    AttnParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.in_dtype = in_dtype;
+    p.o = y;
+    p.out_dtype = out_dtype;
+    p.B = B;
+    p.S = S;
+    p.Hq = H;
+    p.Hkv = H;
+    p.D = D;
+    if (layout == B2A_HEAD_MAJOR) {
+        p.q_sb = (int64_t)H * S * D;
+        p.q_ss = D;
+        p.q_sh = (int64_t)S * D;
+    } else {
+        p.q_sb = (int64_t)S * H * D;
+        p.q_ss = (int64_t)H * D;
+        p.q_sh = D;
+    }
+    p.k_sb = p.q_sb;
+    p.k_ss = p.q_ss;
+    p.k_sh = p.q_sh;
+    p.causal = 0;
+    p.window = 0;
+    p.mask = mask;
+    p.key_len = key_lengths;
+    p.scale = scale;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaSuccess;
+    if (in_dtype == B2A_BFLOAT16) {
+        // same operand rule as the prefill: bf16 inputs are multiplied as fp16
+        const size_t n = (size_t)B * H * S * D;
+        const size_t one = (n * 2 + 255) / 256 * 256;
+        int rc = ensure_buffer(ctx, &ctx->pf_ws, &ctx->pf_ws_bytes, 3 * one, "encoder");
+        if (rc) return rc;
+        char* base = static_cast<char*>(ctx->pf_ws);
+        e = launch_convert(q, in_dtype, base, B2A_FLOAT16, (int64_t)n, ctx->status, s);
+        if (e == cudaSuccess) e = launch_convert(k, in_dtype, base + one, B2A_FLOAT16, (int64_t)n, ctx->status, s);
+        if (e == cudaSuccess) e = launch_convert(v, in_dtype, base + 2 * one, B2A_FLOAT16, (int64_t)n, ctx->status, s);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "conversion kernel launch");
+        p.q = base;
+        p.k = base + one;
+        p.v = base + 2 * one;
+        p.in_dtype = B2A_FLOAT16;
+    }
+    e = attn_tc_supported(p) ? launch_attn_tc(p, s) : launch_attn_simt(p, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "attention kernel launch");
+    return B2A_OK;
+}
+
+// ----------------------------------------------------------------- prefill
+B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype, const void* q, const void* k,
+                               const void* v, void* o, int B, int S, int Hq, int Hkv, int D, float scale, int rope_mode,
+                               double rope_theta, int pos0, int window, void* k_rot_out, void* stream) {
+    if (!ctx) return B2A_EINVAL;
+    if (!valid_dtype(in_dtype) || !valid_dtype(out_dtype))
+        return fail(ctx, B2A_EINVAL, "unsupported element type (in %d, out %d)", in_dtype, out_dtype);
+    if (!q || !k || !v || !o) return fail(ctx, B2A_EINVAL, "q, k, v and o must not be null");
+    int rc = check_heads(ctx, Hq, Hkv);
+    if (rc) return rc;
+    if ((rc = check_head_dim(ctx, D))) return rc;
+    if (B <= 0 || S <= 0) return fail(ctx, B2A_EINVAL, "batch and sequence length must be > 0");
+    if (window < 0) return fail(ctx, B2A_EINVAL, "window must not be negative");
+    if (pos0 < 0) return fail(ctx, B2A_EINVAL, "pos0 must not be negative");
+    if (rope_mode != B2A_ROPE_NONE && rope_mode != B2A_ROPE_NEOX && rope_mode != B2A_ROPE_GEMMA)
+        return fail(ctx, B2A_EINVAL, "unknown rope mode %d", rope_mode);
+    if (rope_mode != B2A_ROPE_NONE && !(rope_theta > 0.0)) return fail(ctx, B2A_EINVAL, "rope theta must be > 0");
+    if (!(scale == scale) || scale <= 0.f) return fail(ctx, B2A_EINVAL, "scale must be a positive number");
+    DeviceGuard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    AttnParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.in_dtype = in_dtype;
+    p.o = o;
+    p.out_dtype = out_dtype;
+    p.B = B;
+    p.S = S;
+    p.Hq = Hq;
+    p.Hkv = Hkv;
+    p.D = D;
+    p.q_sb = (int64_t)S * Hq * D;
+    p.q_ss = (int64_t)Hq * D;
+    p.q_sh = D;
+    p.k_sb = (int64_t)S * Hkv * D;
+    p.k_ss = (int64_t)Hkv * D;
+    p.k_sh = D;
+    p.causal = 1;
+    p.window = window;
+    p.scale = scale;
+
+    // bf16 inputs are multiplied as fp16 tensor-core operands: the rotated q/k,
+    // P and V then carry 11 significant bits instead of 8, which keeps short
+    // causal rows within the 2e-3 tolerance (bf16 -> fp16 is exact inside the
+    // fp16 range; values beyond it raise device status bit 2).
+    const int cdt = in_dtype == B2A_BFLOAT16 ? B2A_FLOAT16 : in_dtype;
+    const size_t ce = dtype_size(cdt);
+    const size_t nq = (size_t)B * S * Hq * D, nk = (size_t)B * S * Hkv * D;
+    auto r256 = [](size_t x) { return (x + 255) / 256 * 256; };
+    const bool rope = rope_mode != B2A_ROPE_NONE;
+    const bool conv = cdt != in_dtype;
+    const size_t table_bytes = rope ? r256((size_t)S * (D / 2) * 16) : 0;
+    const size_t q_bytes = (rope || conv) ? r256(nq * ce) : 0;
+    const bool k_in_out = rope && !conv && k_rot_out != nullptr;  // rotated keys land in k_rot_out directly
+    const size_t k_bytes = ((rope || conv) && !k_in_out) ? r256(nk * ce) : 0;
+    const size_t v_bytes = conv ? r256(nk * ce) : 0;
+    if (table_bytes + q_bytes + k_bytes + v_bytes > 0) {
+        rc = ensure_buffer(ctx, &ctx->pf_ws, &ctx->pf_ws_bytes, table_bytes + q_bytes + k_bytes + v_bytes, "prefill");
+        if (rc) return rc;
+    }
+    char* base = static_cast<char*>(ctx->pf_ws);
+    double2* table = reinterpret_cast<double2*>(base);
+    void* q_c = base + table_bytes;
+    void* k_c = k_in_out ? k_rot_out : base + table_bytes + q_bytes;
+    void* v_c = base + table_bytes + q_bytes + k_bytes;
+    cudaError_t e = cudaSuccess;
+    if (rope) {
+        double inv[kMaxHeadDim / 2];
+        inv_freq_table(rope_theta, D, inv);
+        e = launch_rope_rows_with_table(q, in_dtype, q_c, cdt, B, S, Hq, D, p.q_sb, p.q_ss, p.q_sh, p.q_sb, p.q_ss,
+                                        p.q_sh, pos0, rope_mode, inv, table, true, ctx->status, s);
+        if (e == cudaSuccess)
+            e = launch_rope_rows_with_table(k, in_dtype, k_c, cdt, B, S, Hkv, D, p.k_sb, p.k_ss, p.k_sh, p.k_sb,
+                                            p.k_ss, p.k_sh, pos0, rope_mode, inv, table, false, ctx->status, s);
+        if (e == cudaSuccess && k_rot_out && !k_in_out)  // caller wants rotated keys in its own dtype
+            e = launch_rope_rows_with_table(k, in_dtype, k_rot_out, in_dtype, B, S, Hkv, D, p.k_sb, p.k_ss, p.k_sh,
+                                            p.k_sb, p.k_ss, p.k_sh, pos0, rope_mode, inv, table, false, nullptr, s);
+    } else {
+        if (conv) {
+            e = launch_convert(q, in_dtype, q_c, cdt, (int64_t)nq, ctx->status, s);
+            if (e == cudaSuccess) e = launch_convert(k, in_dtype, k_c, cdt, (int64_t)nk, ctx->status, s);
+        }
+        if (e == cudaSuccess && k_rot_out)
+            e = cudaMemcpyAsync(k_rot_out, k, nk * dtype_size(in_dtype), cudaMemcpyDeviceToDevice, s);
+    }
+    if (e == cudaSuccess && conv) e = launch_convert(v, in_dtype, v_c, cdt, (int64_t)nk, ctx->status, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "rope / conversion kernel launch");
+    if (rope || conv) {
+        p.q = q_c;
+        p.k = k_c;
+    }
+    if (conv) p.v = v_c;
+    p.in_dtype = cdt;
+    e = attn_tc_supported(p) ? launch_attn_tc(p, s) : launch_attn_simt(p, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "attention kernel launch");
+    return B2A_OK;
+}
+
+// ----------------------------------------------------------------- decode
+B2A_API int b2a_decode(b2a_context* ctx, int q_dtype, int cache_dtype, int out_dtype, const void* q_new,
+                       const void* k_new, const void* v_new, void* k_cache, void* v_cache, int kv_layout,
+                       const int32_t* ctx_lens, int B, int Hq, int Hkv, int D, int max_seq, float scale,
+                       int rope_mode, double rope_theta, int window, const float* q_norm_w, const float* k_norm_w,
+                       float norm_eps, void* o, void* stream) {
+    if (!ctx) return B2A_EINVAL;
+    if (!valid_dtype(q_dtype) || !valid_dtype(cache_dtype) || !valid_dtype(out_dtype))
+        return fail(ctx, B2A_EINVAL, "unsupported element type (q %d, cache %d, out %d)", q_dtype, cache_dtype,
+                    out_dtype);
+    if (!q_new || !k_new || !v_new || !k_cache || !v_cache || !ctx_lens || !o)
+        return fail(ctx, B2A_EINVAL, "q_new, k_new, v_new, caches, ctx_lens and o must not be null");
+    int rc = check_heads(ctx, Hq, Hkv);
+    if (rc) return rc;
+    if ((rc = check_head_dim(ctx, D))) return rc;
+    if (B <= 0) return fail(ctx, B2A_EINVAL, "batch must be > 0");
+    if (max_seq <= 0) return fail(ctx, B2A_EINVAL, "max_seq must be > 0");
+    if (window < 0) return fail(ctx, B2A_EINVAL, "window must not be negative");
+    if (kv_layout != B2A_KV_HEAD_MAJOR && kv_layout != B2A_KV_POS_MAJOR)
+        return fail(ctx, B2A_EINVAL, "unknown kv layout %d", kv_layout);
+    if (rope_mode != B2A_ROPE_NONE && rope_mode != B2A_ROPE_NEOX && rope_mode != B2A_ROPE_GEMMA)
+        return fail(ctx, B2A_EINVAL, "unknown rope mode %d", rope_mode);
+    if (rope_mode != B2A_ROPE_NONE && !(rope_theta > 0.0)) return fail(ctx, B2A_EINVAL, "rope theta must be > 0");
+    if ((q_norm_w == nullptr) != (k_norm_w == nullptr))
+        return fail(ctx, B2A_EINVAL, "q_norm_w and k_norm_w must be given together");
+    if (!(scale == scale) || scale <= 0.f) return fail(ctx, B2A_EINVAL, "scale must be a positive number");
+    if (q_norm_w && !(norm_eps >= 0.f)) return fail(ctx, B2A_EINVAL, "norm_eps must not be negative");
+    DeviceGuard guard(ctx->device);
+    DecodeParams p{};
+    p.q = q_new;
+    p.k_new = k_new;
+    p.v_new = v_new;
+    p.q_dtype = q_dtype;
+    p.k_cache = k_cache;
+    p.v_cache = v_cache;
+    p.cache_dtype = cache_dtype;
+    p.stride_b = (int64_t)Hkv * max_seq * D;
+    if (kv_layout == B2A_KV_HEAD_MAJOR) {
+        p.stride_h = (int64_t)max_seq * D;
+        p.stride_pos = D;
+    } else {
+        p.stride_h = D;
+        p.stride_pos = (int64_t)Hkv * D;
+    }
+    p.ctx_lens = ctx_lens;
+    p.B = B;
+    p.Hq = Hq;
+    p.Hkv = Hkv;
+    p.G = Hq / Hkv;
+    p.D = D;
+    p.max_seq = max_seq;
+    p.window = window;
+    p.first_explicit = -1;
+    p.append = 1;
+    p.rope_mode = rope_mode;
+    p.scale = scale;
+    p.q_norm_w = q_norm_w;
+    p.k_norm_w = k_norm_w;
+    p.norm_eps = norm_eps;
+    p.out = o;
+    p.out_dtype = out_dtype;
+    if (rope_mode != B2A_ROPE_NONE) inv_freq_table(rope_theta, D, p.inv_freq);
+    return run_decode(ctx, p, static_cast<cudaStream_t>(stream), true);
+}
+
+// ------------------------------------------------- reference GPU contracts
+B2A_API int b2a_qwen_rope_and_append(b2a_context* ctx, float* q, const float* k, const float* v, float* k_cache,
+                                     float* v_cache, int num_heads, int kv_heads, int head_dim, int pos,
+                                     int max_seq_len, float rope_theta, void* stream) {
+    if (!ctx) return B2A_EINVAL;
+    if (!q || !k || !v || !k_cache || !v_cache) return fail(ctx, B2A_EINVAL, "buffers must not be null");
+    if (num_heads <= 0 || kv_heads <= 0) return fail(ctx, B2A_EINVAL, "numHeads and kvHeads must be positive");
+    int rc = check_head_dim(ctx, head_dim);
+    if (rc) return rc;
+    if (pos < 0 || pos >= max_seq_len) return fail(ctx, B2A_EINVAL, "pos %d outside [0, maxSeqLen=%d)", pos, max_seq_len);
+    if (!(rope_theta > 0.f)) return fail(ctx, B2A_EINVAL, "rope theta must be > 0");
+    DeviceGuard guard(ctx->device);
+    double inv[kMaxHeadDim / 2];
+    inv_freq_table((double)rope_theta, head_dim, inv);
+    cudaError_t e = launch_qwen_rope_append(q, k, v, k_cache, v_cache, num_heads, kv_heads, head_dim, pos, max_seq_len,
+                                            inv, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "rope_and_append launch");
+    return B2A_OK;
+}
+
+B2A_API int b2a_qwen_gqa_attention_decode(b2a_context* ctx, const float* q, const float* k_cache, const float* v_cache,
+                                          float* attn_out, int num_heads, int kv_heads, int head_dim,
+                                          int q_heads_per_kv_head, int seq_len, int max_seq_len, float scale,
+                                          void* stream) {
+    if (!ctx) return B2A_EINVAL;
+    if (!q || !k_cache || !v_cache || !attn_out) return fail(ctx, B2A_EINVAL, "buffers must not be null");
+    int rc = check_heads(ctx, num_heads, kv_heads);
+    if (rc) return rc;
+    if (q_heads_per_kv_head != num_heads / kv_heads)
+        return fail(ctx, B2A_EINVAL, "qHeadsPerKvHead %d != numHeads / kvHeads = %d", q_heads_per_kv_head,
+                    num_heads / kv_heads);
+    if ((rc = check_head_dim(ctx, head_dim))) return rc;
+    if (seq_len <= 0 || seq_len > max_seq_len)
+        return fail(ctx, B2A_EINVAL, "seqLen %d outside [1, maxSeqLen=%d]", seq_len, max_seq_len);
+    if (!(scale == scale) || scale <= 0.f) return fail(ctx, B2A_EINVAL, "scale must be a positive number");
+    DeviceGuard guard(ctx->device);
+    DecodeParams p{};
+    p.q = q;
+    p.q_dtype = B2A_FLOAT32;
+    p.k_cache = const_cast<float*>(k_cache);
+    p.v_cache = const_cast<float*>(v_cache);
+    p.cache_dtype = B2A_FLOAT32;
+    p.stride_b = 0;
+    p.stride_h = (int64_t)max_seq_len * head_dim;
+    p.stride_pos = head_dim;
+    p.ctx_lens = nullptr;
+    p.pos_scalar = seq_len - 1;
+    p.B = 1;
+    p.Hq = num_heads;
+    p.Hkv = kv_heads;
+    p.G = q_heads_per_kv_head;
+    p.D = head_dim;
+    p.max_seq = max_seq_len;
+    p.first_explicit = 0;
+    p.append = 0;
+    p.scale = scale;
+    p.out = attn_out;
+    p.out_dtype = B2A_FLOAT32;
+    return run_decode(ctx, p, static_cast<cudaStream_t>(stream), false);
+}
+
+B2A_API int b2a_gemma_fused_attention_context(b2a_context* ctx, const float* q, const float* keys, const float* values,
+                                              float* ctx_out, int num_heads, int groups_per_kv, int head_dim,
+                                              int kv_dim, int first_valid, int query_pos, float scale, void* stream) {
+    if (!ctx) return B2A_EINVAL;
+    if (!q || !keys || !values || !ctx_out) return fail(ctx, B2A_EINVAL, "buffers must not be null");
+    // Gemma3WarpFusedAttentionContextKernel.context (INF/gemma/Gemma3WarpFusedAttentionContextKernel.java:111-124)
+    if (num_heads <= 0 || groups_per_kv <= 0 || num_heads % groups_per_kv != 0)
+        return fail(ctx, B2A_EINVAL, "numHeads must be a multiple of numKvHeads");
+    if (head_dim > 256)
+        return fail(ctx, B2A_EINVAL, "headDim %d exceeds fused-attention group size 256", head_dim);
+    int rc = check_head_dim(ctx, head_dim);
+    if (rc) return rc;
+    const int n_kv = num_heads / groups_per_kv;
+    if (kv_dim < n_kv * head_dim) return fail(ctx, B2A_EINVAL, "kvDim %d < numKvHeads * headDim", kv_dim);
+    if (query_pos < 0 || first_valid < 0 || first_valid > query_pos)
+        return fail(ctx, B2A_EINVAL, "visible key range [%d, %d] is empty or negative", first_valid, query_pos);
+    if (!(scale == scale) || scale <= 0.f) return fail(ctx, B2A_EINVAL, "scale must be a positive number");
+    DeviceGuard guard(ctx->device);
+    DecodeParams p{};
+    p.q = q;
+    p.q_dtype = B2A_FLOAT32;
+    p.k_cache = const_cast<float*>(keys);
+    p.v_cache = const_cast<float*>(values);
+    p.cache_dtype = B2A_FLOAT32;
+    p.stride_b = 0;
+    p.stride_h = head_dim;
+    p.stride_pos = kv_dim;
+    p.ctx_lens = nullptr;
+    p.pos_scalar = query_pos;
+    p.B = 1;
+    p.Hq = num_heads;
+    p.Hkv = n_kv;
+    p.G = groups_per_kv;
+    p.D = head_dim;
+    p.max_seq = query_pos + 1;
+    p.first_explicit = first_valid;
+    p.append = 0;
+    p.scale = scale;
+    p.out = ctx_out;
+    p.out_dtype = B2A_FLOAT32;
+    return run_decode(ctx, p, static_cast<cudaStream_t>(stream), false);
+}
+
+// ----------------------------------------------------------------- sharding
+B2A_API int b2a_partition_units(int n_units, int n_ranks, const int64_t* unit_cost, int32_t* rank_of_unit) {
+    if (n_units <= 0 || n_ranks <= 0 || !unit_cost || !rank_of_unit) return B2A_EINVAL;
+    if (n_units % n_ranks != 0) return B2A_EINVAL;
+    const int cap = n_units / n_ranks;
+    std::vector<int> order(n_units);
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return unit_cost[a] > unit_cost[b]; });
+    std::vector<int64_t> load(n_ranks, 0);
+    std::vector<int> count(n_ranks, 0);
+    for (int u : order) {
+        int best = -1;
+        for (int r = 0; r < n_ranks; ++r) {
+            if (count[r] >= cap) continue;
+            if (best < 0 || load[r] < load[best]) best = r;
+        }
+        rank_of_unit[u] = best;
+        load[best] += unit_cost[u];
+        ++count[best];
+    }
+    return B2A_OK;
+}
+
+}  // extern "C"

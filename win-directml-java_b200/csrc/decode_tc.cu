@@ -1,0 +1,633 @@
+// decode_tc.cu -- split-KV single-token decode for fp16 / bf16 KV caches.
+//
+// One persistent launch per decode step (one CTA slot per resident CTA).
+// Each CTA
+//   1. plans from the device-resident ctx_lens: the visible keys of every
+//      unit (sequence, kv head, head group of 8) form one key stream, and CTA
+//      c owns the contiguous range [c*R, (c+1)*R) of it (stream-K split:
+//      balanced to one key whatever the length mix);
+//   2. walks the pieces of units inside its range.  Per piece it
+//        - streams K and V tiles of 64 keys with 16-byte cp.async (3-4 stage
+//          ring, padded rows so ldmatrix is bank-conflict free),
+//        - builds the item's q rows in shared memory: optional zero-centred
+//          RMS QK-norm and RoPE at position L (angles in double), and for
+//          the chunk that ends at L the new key/value row, which it writes
+//          to the cache and patches into its own tile (no other item reads
+//          row L, so the append needs no grid-wide ordering),
+//        - computes S^T = K Q^T and O^T += V^T P^T with m16n8k16 warp MMAs:
+//          keys are the M dimension (16 per warp), the G <= 8 query heads of
+//          a kv head the N = 8 dimension, so one K/V byte feeds every head;
+//          online softmax in fp32 (base-2, one exp2 per key and head);
+//        - merges its four warps and either writes the output (whole units)
+//          or a partial (m, l, O) slot (at most two per CTA: a unit cut at
+//          the start and one cut at the end of its range); the last piece of
+//          a unit to finish merges the slots with a log-sum-exp combine and
+//          resets its counter.
+// The arithmetic intensity is 4-7 flop/byte, so the kernel is bound by HBM;
+// warp MMAs are used because they cut the issue count per key ~10x against
+// fp32 FMAs + shuffles (G=7, D=64 would otherwise be issue-bound), not for
+// FLOPs.
+//
+// Semantics follow Qwen2Runtime.processLayerDecode (INF/qwen/Qwen2Runtime.java:723-766),
+// the HLSL decode contracts (WB/windows/QwenAttentionShaders.java:82-263,
+// INF/gemma/Gemma3WarpFusedAttentionContextKernel.java:32-86) and the Gemma
+// decode prologue (INF/gemma/Gemma3ReferenceForwardPass.java:124-142).
+#include <math.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace b2a {
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kTile = 16 * kWarps;  // keys per pipeline stage
+constexpr int kHeads = 8;           // query heads per unit (MMA N)
+
+template <int D>
+struct Geo {
+    static constexpr int kRow = D + 8;  // padded smem row (elements): odd number of 16 B units
+    static constexpr int kStages = D <= 64 ? 4 : 3;
+    static constexpr int kStageElems = 2 * kTile * kRow;  // K tile then V tile
+    static constexpr int kChunks = D / 8;                 // 16-byte chunks per cache row
+    static constexpr size_t kPipeBytes = size_t(kStages) * kStageElems * 2;
+    static constexpr size_t kQBytes = size_t(kHeads) * kRow * 2;
+    static constexpr size_t kNewBytes = size_t(2) * D * 2;
+    static constexpr size_t kVecBytes = size_t(kWarps) * D * 4;
+    static constexpr size_t kCsBytes = size_t(D / 2) * 2 * sizeof(double);
+    static constexpr size_t kPrefixBytes = size_t(kDecodeMaxBatchPerLaunch + 1) * 4;
+    static constexpr size_t kMlBytes = size_t(kWarps) * kHeads * 2 * 4;
+    static constexpr size_t kMergeBytes = size_t(kWarps) * kHeads * D * 4;  // aliases the pipe
+    // merge weights [pieces][kHeads] + [kHeads] sums also alias the pipe
+    static constexpr int kMaxPieces = int((kPipeBytes - kMergeBytes) / (kHeads * 4)) - 1;
+    static_assert(kMergeBytes <= kPipeBytes, "merge scratch must fit in the pipeline buffers");
+    // every region starts on a 16-byte boundary (misc is read as 8-byte words,
+    // cs as doubles, the pipe and q rows by 16-byte cp.async / ldmatrix)
+    static constexpr size_t a16(size_t x) { return (x + 15) / 16 * 16; }
+    static constexpr size_t oQ = a16(kPipeBytes);
+    static constexpr size_t oQlo = a16(oQ + kQBytes);  // low parts of q (bf16 caches only)
+    static constexpr size_t oNew = a16(oQlo + kQBytes);
+    static constexpr size_t oVec = a16(oNew + kNewBytes);
+    static constexpr size_t oCs = a16(oVec + kVecBytes);
+    static constexpr size_t oPrefix = a16(oCs + kCsBytes);
+    static constexpr size_t oMl = a16(oPrefix + kPrefixBytes);
+    static constexpr size_t oMisc = a16(oMl + kMlBytes);
+    static constexpr size_t kTotal = oMisc + 64;
+    static_assert(oMisc % 16 == 0 && oCs % 16 == 0 && oMl % 16 == 0, "aligned shared regions");
+    static_assert(kTotal <= 227 * 1024, "shared memory budget");
+};
+
+__device__ __forceinline__ bool seq_range(const DecodeParams& p, int b, int& L, int& first) {
+    L = p.ctx_lens ? p.ctx_lens[b] : p.pos_scalar;
+    if (L < 0 || L >= p.max_seq) {
+        L = 0;
+        first = 0;
+        return false;
+    }
+    if (p.first_explicit >= 0) first = min(p.first_explicit, L);
+    else if (p.window > 0) first = max(0, L - p.window + 1);
+    else first = 0;
+    return true;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Loads one head vector, applies the optional QK-norm, and writes it (rotated
+// when requested) as float into vec[0..D).  Whole warp; vec is warp-private.
+template <int D>
+__device__ __forceinline__ void prep_head(const DecodeParams& p, const void* src, int64_t off, int dtype,
+                                          const float* norm_w, bool rope, const double* cs, float* vec,
+                                          int lane) {
+    double ss = 0.0;
+    float x[D / 32];
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) {
+        x[j] = load_as_float(src, off + lane + 32 * j, dtype);
+        ss += (double)x[j] * (double)x[j];
+    }
+    if (norm_w != nullptr) {
+        // Gemma3ReferenceMath.rmsNormZeroCentered: double sum of squares,
+        // float rms, (float)(x*rms * (1 + w)) (INF/gemma/Gemma3ReferenceMath.java:32-40).
+        ss = warp_sum_d(ss);
+        const float rms = (float)(1.0 / sqrt(__dadd_rn(ss / (double)D, (double)p.norm_eps)));
+#pragma unroll
+        for (int j = 0; j < D / 32; ++j) {
+            const int d = lane + 32 * j;
+            x[j] = (float)__dmul_rn((double)__fmul_rn(x[j], rms), __dadd_rn(1.0, (double)norm_w[d]));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) vec[lane + 32 * j] = x[j];
+    __syncwarp();
+    if (rope) {
+        constexpr int H = D / 2;
+        float y0[(H + 31) / 32], y1[(H + 31) / 32];
+#pragma unroll
+        for (int j = 0; j < (H + 31) / 32; ++j) {
+            const int i = lane + 32 * j;
+            if (i < H) {
+                const float a = vec[i], b = vec[i + H];
+                const double c = cs[2 * i], s = cs[2 * i + 1];
+                if (p.rope_mode == 2) {
+                    // applyRopeHalf: double products, float result (INF/gemma/Gemma3ReferenceMath.java:76-81)
+                    y0[j] = (float)__dsub_rn(__dmul_rn((double)a, c), __dmul_rn((double)b, s));
+                    y1[j] = (float)__dadd_rn(__dmul_rn((double)b, c), __dmul_rn((double)a, s));
+                } else {
+                    // DecoderOnlyRotaryEmbedding.rotate: float cos/sin, float products
+                    // (INF/decoderonly/DecoderOnlyRotaryEmbedding.java:61-67)
+                    const float cf = (float)c, sf = (float)s;
+                    y0[j] = __fsub_rn(__fmul_rn(a, cf), __fmul_rn(b, sf));
+                    y1[j] = __fadd_rn(__fmul_rn(a, sf), __fmul_rn(b, cf));
+                }
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < (H + 31) / 32; ++j) {
+            const int i = lane + 32 * j;
+            if (i < H) {
+                vec[i] = y0[j];
+                vec[i + H] = y1[j];
+            }
+        }
+    }
+    __syncwarp();
+}
+
+template <int D, typename T>
+__global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_constant__ DecodeParams p) {
+    using Gm = Geo<D>;
+    constexpr int kRow = Gm::kRow;
+    constexpr int kStages = Gm::kStages;
+    extern __shared__ __align__(128) unsigned char smem[];
+    T* pipe = reinterpret_cast<T*>(smem);
+    T* q_s = reinterpret_cast<T*>(smem + Gm::oQ);
+    T* qlo_s = reinterpret_cast<T*>(smem + Gm::oQlo);
+    // bf16 operands carry 8 mantissa bits: q and P are split into hi + lo
+    // bf16 parts and both are multiplied, which restores ~16-bit operand
+    // precision at twice the (idle) tensor work.
+    constexpr bool kSplit = std::is_same<T, __nv_bfloat16>::value;
+    T* knew_s = reinterpret_cast<T*>(smem + Gm::oNew);
+    T* vnew_s = knew_s + D;
+    float* vec_all = reinterpret_cast<float*>(smem + Gm::oVec);
+    double* cs_s = reinterpret_cast<double*>(smem + Gm::oCs);
+    int* prefix = reinterpret_cast<int*>(smem + Gm::oPrefix);
+    float* ml_s = reinterpret_cast<float*>(smem + Gm::oMl);
+    int* misc = reinterpret_cast<int*>(smem + Gm::oMisc);
+    float* merge_s = reinterpret_cast<float*>(smem);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    float* vec = vec_all + warp * D;
+
+    // ---------------------------------------------------------------- plan
+    // Stream-K split: the visible keys of all units (sequence, kv head, head
+    // group) form one key stream; CTA c owns the contiguous range
+    // [c*R, (c+1)*R), R = ceil(total / gridDim.x).  Work is balanced to one
+    // key, and a unit is cut only where CTA ranges cross it.
+    // prefix[b] = visible keys of sequences < b (int32: the host keeps each
+    // launch's total below 2^31).
+    {
+        const int per = (p.B + kThreads - 1) / kThreads;
+        const int b0 = min(p.B, tid * per), b1 = min(p.B, b0 + per);
+        int run = 0, bad = 0;
+        for (int b = b0; b < b1; ++b) {
+            int L, first;
+            if (!seq_range(p, b, L, first)) bad = 1;
+            run += L - first + 1;
+        }
+        if (bad && blockIdx.x == 0) atomicOr(p.status, 1);
+        int incl = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (lane == 31) misc[warp] = incl;
+        __syncthreads();
+        int warp_off = 0;
+        for (int w = 0; w < warp; ++w) warp_off += misc[w];
+        int acc = warp_off + incl - run;
+        for (int b = b0; b < b1; ++b) {
+            prefix[b] = acc;
+            int L, first;
+            seq_range(p, b, L, first);
+            acc += L - first + 1;
+        }
+        if (tid == kThreads - 1) prefix[p.B] = warp_off + incl;
+        __syncthreads();
+    }
+    const int per_chunk = p.Hkv * p.n_hg;  // units per sequence
+    const long long total = (long long)prefix[p.B] * per_chunk;
+    const long long R = (total + gridDim.x - 1) / gridDim.x;
+    if (2 * (long long)gridDim.x > p.item_capacity) {  // never write past the partial slots
+        if (tid == 0 && blockIdx.x == 0) atomicOr(p.status, 2);
+        return;
+    }
+    const float scale_log2 = p.scale * kLog2e;
+    constexpr float kNegInf = -INFINITY;
+    const long long range_lo = (long long)blockIdx.x * R;
+    const long long range_hi = min(total, range_lo + R);
+
+    for (long long pos = range_lo; pos < range_hi;) {
+        // unit containing pos: sequence b (prefix search), then (kv head, head group)
+        int lo = 0, hi = p.B - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if ((long long)prefix[mid] * per_chunk <= pos) lo = mid;
+            else hi = mid - 1;
+        }
+        const int b = lo;
+        int L, first;
+        const bool ok = seq_range(p, b, L, first);
+        const int n_b = L - first + 1;
+        const long long seq_base = (long long)prefix[b] * per_chunk;
+        const int r = (int)((pos - seq_base) / n_b);
+        const long long u_start = seq_base + (long long)r * n_b, u_end = u_start + n_b;
+        const long long piece_end = min(range_hi, u_end);
+        const int kvh = r / p.n_hg, hg = r - kvh * p.n_hg;
+        const int k0 = first + (int)(pos - u_start);
+        const int k1 = first + (int)(piece_end - u_start);
+        const int c0 = (int)(u_start / R), c1 = (int)((u_end - 1) / R);
+        const int n_split = c1 - c0 + 1;                    // pieces of this unit
+        const int my_slot = 2 * blockIdx.x + (pos == range_lo ? 0 : 1);
+        const int unit = b * per_chunk + r;
+        pos = piece_end;
+        const int h0 = kvh * p.G + hg * kHeads;
+        const int nh = min(kHeads, p.G - hg * kHeads);
+
+        if (!ok) {
+            for (int e = tid; e < nh * D; e += kThreads)
+                store_from_float(p.out, ((int64_t)b * p.Hq + h0 + e / D) * D + e % D, __int_as_float(0x7fc00000),
+                                 p.out_dtype);
+            continue;
+        }
+
+        const T* kc = static_cast<const T*>(p.k_cache) + b * p.stride_b + kvh * p.stride_h;
+        const T* vc = static_cast<const T*>(p.v_cache) + b * p.stride_b + kvh * p.stride_h;
+        const int n_tiles = (k1 - k0 + kTile - 1) / kTile;
+        const bool has_new = p.append && k1 == L + 1;
+
+        auto load_tile = [&](int tile, int stage) {
+            const int ts = k0 + tile * kTile;
+            T* ks = pipe + stage * Gm::kStageElems;
+            T* vs = ks + kTile * kRow;
+#pragma unroll 4
+            for (int x = tid; x < kTile * Gm::kChunks; x += kThreads) {
+                const int row = x / Gm::kChunks, cc = x - row * Gm::kChunks;
+                const int key = ts + row;
+                const bool in = key < k1;
+                const int64_t off = (int64_t)(in ? key : k0) * p.stride_pos + cc * 8;
+                cp_async_16(smem_u32(ks + row * kRow + cc * 8), kc + off, in ? 16 : 0);
+                cp_async_16(smem_u32(vs + row * kRow + cc * 8), vc + off, in ? 16 : 0);
+            }
+        };
+#pragma unroll
+        for (int s = 0; s < kStages - 1; ++s) {
+            if (s < n_tiles) load_tile(s, s);
+            cp_async_commit();
+        }
+
+        // ------------------------------------------------ prologue (q, new k/v)
+        const bool rope = p.append && p.rope_mode != 0;
+        if (rope) {
+            for (int i = tid; i < D / 2; i += kThreads) {
+                double sn, cn;
+                sincos((double)L * p.inv_freq[i], &sn, &cn);
+                cs_s[2 * i] = cn;
+                cs_s[2 * i + 1] = sn;
+            }
+        }
+        __syncthreads();
+        for (int hl = warp; hl < kHeads; hl += kWarps) {
+            T* qrow = q_s + hl * kRow;
+            T* qlo = qlo_s + hl * kRow;
+            if (hl >= nh) {
+                for (int d = lane; d < D; d += 32) qrow[d] = qlo[d] = Elem<T>::from_float(0.f);
+                continue;
+            }
+            prep_head<D>(p, p.q, ((int64_t)b * p.Hq + h0 + hl) * D, p.q_dtype, p.append ? p.q_norm_w : nullptr,
+                         rope, cs_s, vec, lane);
+            for (int d = lane; d < D; d += 32) {
+                const T hi = Elem<T>::from_float(vec[d]);
+                qrow[d] = hi;
+                if (kSplit) qlo[d] = Elem<T>::from_float(vec[d] - Elem<T>::to_float(hi));
+            }
+            __syncwarp();
+        }
+        if (has_new) {
+            if (warp == 0) {
+                prep_head<D>(p, p.k_new, ((int64_t)b * p.Hkv + kvh) * D, p.q_dtype, p.k_norm_w, rope, cs_s, vec,
+                             lane);
+                T* dst = static_cast<T*>(p.k_cache) + b * p.stride_b + kvh * p.stride_h + (int64_t)L * p.stride_pos;
+                for (int d = lane; d < D; d += 32) {
+                    const T v = Elem<T>::from_float(vec[d]);
+                    knew_s[d] = v;
+                    if (hg == 0) dst[d] = v;
+                }
+            } else if (warp == 1) {
+                T* dst = static_cast<T*>(p.v_cache) + b * p.stride_b + kvh * p.stride_h + (int64_t)L * p.stride_pos;
+                for (int d = lane; d < D; d += 32) {
+                    const T v = Elem<T>::from_float(load_as_float(p.v_new, ((int64_t)b * p.Hkv + kvh) * D + d, p.q_dtype));
+                    vnew_s[d] = v;
+                    if (hg == 0) dst[d] = v;
+                }
+            }
+        }
+        __syncthreads();
+
+        uint32_t qb[D / 16][2];
+        uint32_t qbl[kSplit ? D / 16 : 1][2];
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+            const T* base = q_s + g * kRow + 16 * ks + 2 * t;
+            qb[ks][0] = *reinterpret_cast<const uint32_t*>(base);
+            qb[ks][1] = *reinterpret_cast<const uint32_t*>(base + 8);
+            if constexpr (kSplit) {
+                const T* bl = qlo_s + g * kRow + 16 * ks + 2 * t;
+                qbl[ks][0] = *reinterpret_cast<const uint32_t*>(bl);
+                qbl[ks][1] = *reinterpret_cast<const uint32_t*>(bl + 8);
+            }
+        }
+
+        // ------------------------------------------------------- main loop
+        float acc[D / 16][4];
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
+        float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
+        const int wrow = warp * 16;
+
+        for (int tile = 0; tile < n_tiles; ++tile) {
+            cp_async_wait<kStages - 2>();
+            __syncthreads();
+            const int stage = tile % kStages;
+            T* ks = pipe + stage * Gm::kStageElems;
+            T* vs = ks + kTile * kRow;
+            const int ts = k0 + tile * kTile;
+            if (has_new && L >= ts && L < ts + kTile) {
+                const int row = L - ts;
+                for (int d = tid; d < D; d += kThreads) {
+                    ks[row * kRow + d] = knew_s[d];
+                    vs[row * kRow + d] = vnew_s[d];
+                }
+                __syncthreads();
+            }
+            {
+                const int nt = tile + kStages - 1;
+                if (nt < n_tiles) load_tile(nt, nt % kStages);
+                cp_async_commit();
+            }
+            if (ts + wrow >= k1) continue;  // this warp's 16 rows are all past the chunk
+
+            float s[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t ka = smem_u32(ks + (wrow + (lane & 15)) * kRow + 8 * (lane >> 4));
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                uint32_t a[4];
+                ldmatrix_x4(a[0], a[1], a[2], a[3], ka + kk * 32);
+                Mma<T>::run(s, a, qb[kk][0], qb[kk][1]);
+                if constexpr (kSplit) Mma<T>::run(s, a, qbl[kk][0], qbl[kk][1]);
+            }
+            const int key_a = ts + wrow + g, key_b = key_a + 8;
+            const float sa0 = key_a < k1 ? s[0] * scale_log2 : kNegInf;
+            const float sa1 = key_a < k1 ? s[1] * scale_log2 : kNegInf;
+            const float sb0 = key_b < k1 ? s[2] * scale_log2 : kNegInf;
+            const float sb1 = key_b < k1 ? s[3] * scale_log2 : kNegInf;
+            float mt0 = fmaxf(sa0, sb0), mt1 = fmaxf(sa1, sb1);
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) {
+                mt0 = fmaxf(mt0, __shfl_xor_sync(0xffffffffu, mt0, o));
+                mt1 = fmaxf(mt1, __shfl_xor_sync(0xffffffffu, mt1, o));
+            }
+            const float mn0 = fmaxf(m0, mt0), mn1 = fmaxf(m1, mt1);
+            const float base0 = mn0 == kNegInf ? 0.f : mn0;
+            const float base1 = mn1 == kNegInf ? 0.f : mn1;
+            const float c0 = fast_exp2(m0 - base0), c1 = fast_exp2(m1 - base1);
+            const float pa0 = fast_exp2(sa0 - base0), pa1 = fast_exp2(sa1 - base1);
+            const float pb0 = fast_exp2(sb0 - base0), pb1 = fast_exp2(sb1 - base1);
+            l0 = l0 * c0 + pa0 + pb0;
+            l1 = l1 * c1 + pa1 + pb1;
+            m0 = mn0;
+            m1 = mn1;
+#pragma unroll
+            for (int mt = 0; mt < D / 16; ++mt) {
+                acc[mt][0] *= c0;
+                acc[mt][1] *= c1;
+                acc[mt][2] *= c0;
+                acc[mt][3] *= c1;
+            }
+            const uint32_t ph0 = Elem<T>::pack(pa0, pa1), ph1 = Elem<T>::pack(pb0, pb1);
+            const uint32_t pf0 = movmatrix_trans(ph0);
+            const uint32_t pf1 = movmatrix_trans(ph1);
+            uint32_t pl0 = 0, pl1 = 0;
+            if constexpr (kSplit) {
+                const T* h0p = reinterpret_cast<const T*>(&ph0);
+                const T* h1p = reinterpret_cast<const T*>(&ph1);
+                pl0 = movmatrix_trans(Elem<T>::pack(pa0 - Elem<T>::to_float(h0p[0]), pa1 - Elem<T>::to_float(h0p[1])));
+                pl1 = movmatrix_trans(Elem<T>::pack(pb0 - Elem<T>::to_float(h1p[0]), pb1 - Elem<T>::to_float(h1p[1])));
+            }
+            const uint32_t va = smem_u32(vs + (wrow + (lane & 7) + 8 * (lane >> 4)) * kRow + 8 * ((lane >> 3) & 1));
+#pragma unroll
+            for (int mt = 0; mt < D / 16; ++mt) {
+                uint32_t a[4];
+                ldmatrix_x4_trans(a[0], a[1], a[2], a[3], va + mt * 32);
+                Mma<T>::run(acc[mt], a, pf0, pf1);
+                if constexpr (kSplit) Mma<T>::run(acc[mt], a, pl0, pl1);
+            }
+        }
+        cp_async_wait<0>();
+        __syncthreads();  // pipeline drained: merge_s may alias it now
+
+        // ------------------------------------------------------- epilogue
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+        }
+        {
+            float* mw = merge_s + warp * kHeads * D;
+#pragma unroll
+            for (int mt = 0; mt < D / 16; ++mt) {
+                const int d0 = 16 * mt + g;
+                mw[(2 * t) * D + d0] = acc[mt][0];
+                mw[(2 * t + 1) * D + d0] = acc[mt][1];
+                mw[(2 * t) * D + d0 + 8] = acc[mt][2];
+                mw[(2 * t + 1) * D + d0 + 8] = acc[mt][3];
+            }
+            if (g == 0) {
+                ml_s[(warp * kHeads + 2 * t) * 2 + 0] = m0;
+                ml_s[(warp * kHeads + 2 * t) * 2 + 1] = l0;
+                ml_s[(warp * kHeads + 2 * t + 1) * 2 + 0] = m1;
+                ml_s[(warp * kHeads + 2 * t + 1) * 2 + 1] = l1;
+            }
+        }
+        __syncthreads();
+        float* slot = p.partials + (int64_t)my_slot * kHeads * (D + 2);
+        for (int e = tid; e < kHeads * D; e += kThreads) {
+            const int hl = e / D, d = e - hl * D;
+            if (hl >= nh) continue;
+            float M = kNegInf;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) M = fmaxf(M, ml_s[(w * kHeads + hl) * 2]);
+            const float base = M == kNegInf ? 0.f : M;
+            float o = 0.f, l = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const float f = fast_exp2(ml_s[(w * kHeads + hl) * 2] - base);
+                o += f * merge_s[(w * kHeads + hl) * D + d];
+                l += f * ml_s[(w * kHeads + hl) * 2 + 1];
+            }
+            if (n_split == 1) {
+                store_from_float(p.out, ((int64_t)b * p.Hq + h0 + hl) * D + d, o / l, p.out_dtype);
+            } else {
+                slot[hl * D + d] = o;
+                if (d == 0) {
+                    slot[kHeads * D + hl] = base;
+                    slot[kHeads * D + kHeads + hl] = l;
+                }
+            }
+        }
+        if (n_split > 1) {
+            __threadfence();
+            __syncthreads();
+            int* counter = p.counters + unit;
+            if (tid == 0) misc[8] = (atomicAdd(counter, 1) == n_split - 1);
+            __syncthreads();
+            if (misc[8]) {
+                // Last piece of the unit: log-sum-exp combine of its n_split
+                // partial slots.  The piece of CTA c sits in slot 2c, or 2c+1
+                // when the unit starts inside c's range after its first piece.
+                __threadfence();
+                float* wgt = merge_s + kWarps * kHeads * D;  // [n_split][kHeads] weights
+                float* lsum = wgt + n_split * kHeads;         // [kHeads]
+                auto slot_of = [&](int c) {
+                    const int sub = (c == c0 && u_start != (long long)c0 * R) ? 1 : 0;
+                    return p.partials + (int64_t)(2 * c + sub) * kHeads * (D + 2);
+                };
+                for (int e = tid; e < n_split * kHeads; e += kThreads)
+                    wgt[e] = __ldcg(slot_of(c0 + e / kHeads) + kHeads * D + e % kHeads);
+                __syncthreads();
+                if (tid < kHeads) {
+                    float M = kNegInf;
+                    for (int c = 0; c < n_split; ++c) M = fmaxf(M, wgt[c * kHeads + tid]);
+                    float l = 0.f;
+                    for (int c = 0; c < n_split; ++c) {
+                        const float f = fast_exp2(wgt[c * kHeads + tid] - M);
+                        wgt[c * kHeads + tid] = f;
+                        l += f * __ldcg(slot_of(c0 + c) + kHeads * D + kHeads + tid);
+                    }
+                    lsum[tid] = l;
+                }
+                __syncthreads();
+                constexpr int kPer = kHeads * D / kThreads;  // output elements per thread
+                float o[kPer];
+#pragma unroll
+                for (int j = 0; j < kPer; ++j) o[j] = 0.f;
+                for (int c = 0; c < n_split; ++c) {
+                    const float* sl = slot_of(c0 + c);
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j) {
+                        const int e = tid + j * kThreads;
+                        o[j] += wgt[c * kHeads + e / D] * __ldcg(sl + e);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < kPer; ++j) {
+                    const int e = tid + j * kThreads;
+                    const int hl = e / D, d = e - hl * D;
+                    if (hl < nh)
+                        store_from_float(p.out, ((int64_t)b * p.Hq + h0 + hl) * D + d, o[j] / lsum[hl],
+                                         p.out_dtype);
+                }
+                if (tid == 0) *counter = 0;
+            }
+        }
+        __syncthreads();  // shared buffers are reused by the next piece
+    }
+}
+
+struct LaunchInfo {
+    int grid = 0;
+    size_t smem = 0;
+};
+
+template <int D, typename T>
+LaunchInfo launch_info(int device) {
+    static std::once_flag once;
+    static LaunchInfo info;
+    static cudaError_t err = cudaSuccess;
+    std::call_once(once, [&] {
+        auto kern = decode_tc_kernel<D, T>;
+        info.smem = Geo<D>::kTotal;
+        err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)info.smem);
+        int occ = 0, sms = 0;
+        if (err == cudaSuccess) err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, info.smem);
+        if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        info.grid = occ * sms;
+        if (info.grid > Geo<D>::kMaxPieces) info.grid = Geo<D>::kMaxPieces;  // merge weights fit in smem
+    });
+    if (err != cudaSuccess) return LaunchInfo{};
+    return info;
+}
+
+template <typename F>
+bool dispatch_dim(int D, F&& f) {
+    switch (D) {
+        case 64: f(std::integral_constant<int, 64>{}); return true;
+        case 96: f(std::integral_constant<int, 96>{}); return true;
+        case 128: f(std::integral_constant<int, 128>{}); return true;
+        case 256: f(std::integral_constant<int, 256>{}); return true;
+        default: return false;
+    }
+}
+
+}  // namespace
+
+bool decode_tc_supported(int D, int cache_dtype) {
+    return (cache_dtype == kF16 || cache_dtype == kBF16) && (D == 64 || D == 96 || D == 128 || D == 256);
+}
+
+void decode_tc_workspace(int device, int B, int Hkv, int n_hg, int D, int cache_dtype, int* target_items,
+                         int* item_capacity, size_t* partial_bytes) {
+    int grid = 0;
+    dispatch_dim(D, [&](auto dc) {
+        constexpr int kD = decltype(dc)::value;
+        grid = cache_dtype == kBF16 ? launch_info<kD, __nv_bfloat16>(device).grid
+                                    : launch_info<kD, __half>(device).grid;
+    });
+    if (grid <= 0) grid = 148;
+    (void)B;
+    (void)Hkv;
+    (void)n_hg;
+    *target_items = grid;
+    *item_capacity = 2 * grid;  // two partial slots per CTA
+    *partial_bytes = (size_t)(*item_capacity) * kHeads * (D + 2) * sizeof(float);
+}
+
+cudaError_t launch_decode_tc(const DecodeParams& p, int device, cudaStream_t stream) {
+    cudaError_t err = cudaErrorInvalidValue;
+    dispatch_dim(p.D, [&](auto dc) {
+        constexpr int kD = decltype(dc)::value;
+        if (p.cache_dtype == kBF16) {
+            const LaunchInfo li = launch_info<kD, __nv_bfloat16>(device);
+            if (li.grid <= 0) { err = cudaErrorInvalidConfiguration; return; }
+            decode_tc_kernel<kD, __nv_bfloat16><<<li.grid, kThreads, li.smem, stream>>>(p);
+        } else {
+            const LaunchInfo li = launch_info<kD, __half>(device);
+            if (li.grid <= 0) { err = cudaErrorInvalidConfiguration; return; }
+            decode_tc_kernel<kD, __half><<<li.grid, kThreads, li.smem, stream>>>(p);
+        }
+        err = cudaGetLastError();
+    });
+    return err;
+}
+
+}  // namespace b2a

@@ -1,0 +1,98 @@
+// internal.h -- launch parameters and launcher declarations shared between the
+// C-ABI layer (api.cpp) and the CUDA translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b2a {
+
+constexpr int kMaxHeadDim = 256;
+constexpr int kDecodeMaxBatchPerLaunch = 2048;
+
+// One decode step (or one attention over an existing cache when append == 0).
+struct DecodeParams {
+    const void* q;       // [B][Hq][D] q_dtype
+    const void* k_new;   // [B][Hkv][D] q_dtype (append mode)
+    const void* v_new;   // [B][Hkv][D] q_dtype (append mode)
+    int q_dtype;
+    void* k_cache;       // cache_dtype
+    void* v_cache;
+    int cache_dtype;
+    int64_t stride_b, stride_h, stride_pos;  // cache strides in elements
+    const int* ctx_lens; // device [B]; NULL -> pos_scalar for every sequence
+    int pos_scalar;
+    int B, Hq, Hkv, G, D, max_seq;
+    int window;          // > 0: sliding window
+    int first_explicit;  // >= 0: first visible key (overrides window)
+    int append;          // 1: norm + rope + append new k/v at position L, attend [first, L]
+                         // 0: attend [first, L] of the cache with q as given
+    int rope_mode;       // 0 none, 1 NeoX (float rotation), 2 Gemma (double rotation)
+    float scale;
+    const float* q_norm_w;
+    const float* k_norm_w;
+    float norm_eps;
+    void* out;           // [B][Hq][D] out_dtype
+    int out_dtype;
+    // split-KV workspace
+    float* partials;
+    int* counters;       // [B * Hkv * n_hg], zero between launches
+    int* status;         // device error flags (bit 0: ctx_len out of range)
+    int n_hg;            // head groups of 8 per kv head
+    int target_items;
+    int item_capacity;
+    double inv_freq[kMaxHeadDim / 2];
+};
+
+// Tensor-core split-KV decode for 16-bit caches; returns false when the shape
+// has no tensor-core instantiation (caller then uses the generic kernel).
+bool decode_tc_supported(int D, int cache_dtype);
+// Workspace geometry of the tensor-core decode for a batch of B sequences.
+void decode_tc_workspace(int device, int B, int Hkv, int n_hg, int D, int cache_dtype, int* target_items,
+                         int* item_capacity, size_t* partial_bytes);
+cudaError_t launch_decode_tc(const DecodeParams& p, int device, cudaStream_t stream);
+
+// Generic warp-per-head decode: any even D <= 256, any cache dtype.
+cudaError_t launch_decode_simt(const DecodeParams& p, cudaStream_t stream);
+
+// Qwen rope_and_append contract (float32, single sequence).
+cudaError_t launch_qwen_rope_append(float* q, const float* k, const float* v, float* k_cache, float* v_cache,
+                                    int num_heads, int kv_heads, int head_dim, int pos, int max_seq,
+                                    const double* inv_freq, cudaStream_t stream);
+
+// Attention over whole sequences (prefill / encoder).
+struct AttnParams {
+    const void* q;   // rotated already when the caller wants RoPE
+    const void* k;
+    const void* v;
+    int in_dtype;
+    void* o;
+    int out_dtype;
+    int B, S, Hq, Hkv, D;
+    // element strides: [b][s][h][d] addressing for q/o and k/v
+    int64_t q_sb, q_ss, q_sh;
+    int64_t k_sb, k_ss, k_sh;
+    int causal;
+    int window;
+    const float* mask;        // additive [B][S] or NULL
+    const int32_t* key_len;   // [B] or NULL
+    float scale;
+};
+
+cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t stream);
+bool attn_tc_supported(const AttnParams& p);
+cudaError_t launch_attn_tc(const AttnParams& p, cudaStream_t stream);
+
+// RoPE pre-pass: dst[b][s][h][:] = rotate(src[b][s][h][:], pos0 + s); dst may alias src.
+// `table` holds S * D/2 (cos, sin) pairs; build_table == false reuses it.
+cudaError_t launch_rope_rows_with_table(const void* src, int src_dtype, void* dst, int dst_dtype, int B, int S, int H,
+                                        int D, int64_t sb, int64_t ss, int64_t sh, int64_t db, int64_t ds, int64_t dh,
+                                        int pos0, int rope_mode, const double* inv_freq, double2* table,
+                                        bool build_table, int* status, cudaStream_t stream);
+
+// Element-type conversion of n contiguous elements; sets status bit 2 when a
+// finite value overflows the destination type.
+cudaError_t launch_convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n, int* status,
+                           cudaStream_t stream);
+
+}  // namespace b2a
