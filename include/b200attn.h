@@ -204,6 +204,27 @@ B2A_API int b2a_decode(b2a_context* ctx, int q_dtype, int cache_dtype, int out_d
                        const float* q_norm_w, const float* k_norm_w, float norm_eps,
                        void* o, void* stream);
 
+/* The b2a_decode step for callers that cannot allocate device memory: hosts
+ * whose GPU memory belongs to another allocator (a JVM or serving runtime
+ * that owns an arena or caching pool), where a cudaMalloc outside that pool
+ * can fail and cudaMalloc/cudaFree would synchronise the device.  No
+ * counterpart exists in the reference.  Same arguments and results as
+ * b2a_decode, without a context: it runs on the current CUDA device and
+ * allocates nothing; its scratch is a fixed 4 MiB static device array per GPU,
+ * held until the process exits.  The first call on a device resolves that
+ * array's address; make it before any stream capture.  Limits: fp16/bf16
+ * caches, head_dim 64/96/128/256, batch <= 2048 and
+ * batch * Hkv * ceil((Hq/Hkv)/8) <= 16384; larger requests fail with
+ * B2A_EINVAL / B2A_ENOTSUP and a message in b2a_last_error(NULL, ...).
+ * All calls share the scratch: calls whose kernels overlap on the GPU race,
+ * so serialise them (one stream).  An out-of-range ctx_lens entry gives NaN
+ * outputs for that sequence; there is no device-status query. */
+B2A_API int b2a_decode_noalloc(int q_dtype, int cache_dtype, int out_dtype, const void* q_new, const void* k_new,
+                               const void* v_new, void* k_cache, void* v_cache, int kv_layout,
+                               const int32_t* ctx_lens, int B, int Hq, int Hkv, int D, int max_seq, float scale,
+                               int rope_mode, double rope_theta, int window, const float* q_norm_w,
+                               const float* k_norm_w, float norm_eps, void* o, void* stream);
+
 /* ------------------------------------------- reference GPU contracts, 1:1 */
 
 /* ROPE_AND_APPEND_HLSL (WB/windows/QwenAttentionShaders.java:82-135), root

@@ -165,6 +165,11 @@ int run_decode(b2a_context* ctx, DecodeParams& p, cudaStream_t stream, bool allo
 
 }  // namespace
 
+namespace b2a {
+// Message for b2a_last_error(NULL, ...) from entry points that take no context.
+void set_thread_error(const char* msg) { g_create_error = msg ? msg : ""; }
+}  // namespace b2a
+
 extern "C" {
 
 B2A_API const char* b2a_status_string(int status) {

@@ -90,6 +90,9 @@ cudaError_t launch_rope_rows_with_table(const void* src, int src_dtype, void* ds
                                         int pos0, int rope_mode, const double* inv_freq, double2* table,
                                         bool build_table, int* status, cudaStream_t stream);
 
+// Sets the message b2a_last_error(NULL, ...) returns on this thread.
+void set_thread_error(const char* msg);
+
 // Element-type conversion of n contiguous elements; sets status bit 2 when a
 // finite value overflows the destination type.
 cudaError_t launch_convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n, int* status,
