@@ -559,7 +559,7 @@ def main():
         roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tflops, "unit": "TFLOP/s",
                 "frac": round(achieved / tflops, 4), "peak_source": src + " (bf16_tflops, burst)",
                 "flops_per_step": w.flops(), "traffic": None}
-    traffic_file = os.path.join(REPO, "profiles", f"traffic_{args.workload}.json")
+    traffic_file = os.path.join(REPO, "profiles", f"decode_tc_kernel_{args.workload}_traffic.txt")
     if os.path.exists(traffic_file):
         try:
             roof["traffic"] = json.load(open(traffic_file)).get("dram_bytes_per_step")
