@@ -98,6 +98,14 @@ def test_encoder_minilm_config_full_size(ctx, layout):
     assert_close(got, want, what="minilm encoder")
 
 
+@pytest.mark.parametrize("layout,D", [(0, 64), (1, 96), (1, 128)])
+def test_encoder_ragged_length_tensor_core_dims(ctx, layout, D):
+    # head_dim 64/96/128 run on the tcgen05 kernel; S = 300 leaves a ragged last tile
+    got, want = _encoder_case(ctx, B=3, H=2, S=300, D=D, dtype=oracle.F16, lens=[300, 129, 7], layout=layout,
+                              seed=500 + D)
+    assert_close(got, want, what=f"encoder D={D}")
+
+
 def test_encoder_zero_and_full_lengths(ctx):
     # a text with no valid key averages V (softmax of equal -1e9 scores), as the reference does
     got, want = _encoder_case(ctx, B=3, H=2, S=64, D=32, dtype=oracle.F16, lens=[0, 64, 1], layout=1, seed=300)

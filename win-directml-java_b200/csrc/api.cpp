@@ -112,6 +112,14 @@ int check_head_dim(b2a_context* ctx, int D) {
     return B2A_OK;
 }
 
+// Whole-sequence attention: the tcgen05 kernel where its shape rules hold,
+// else the warp-MMA kernel (16-bit, head_dim 32..128), else the generic one.
+cudaError_t launch_attention(b2a_context* ctx, const AttnParams& p, cudaStream_t s) {
+    if (attn_tcgen05_supported(p)) return launch_attn_tcgen05(p, ctx->status, s);
+    if (attn_tc_supported(p)) return launch_attn_tc(p, s);
+    return launch_attn_simt(p, s);
+}
+
 int run_decode(b2a_context* ctx, DecodeParams& p, cudaStream_t stream, bool allow_tc) {
     // 16-byte row loads need 16-byte aligned cache bases and row strides
     const bool aligned = ((uintptr_t)p.k_cache % 16 == 0) && ((uintptr_t)p.v_cache % 16 == 0) &&
@@ -299,6 +307,7 @@ B2A_API int b2a_check_device_status(b2a_context* ctx, void* stream) {
     if (st[0] & 1) msg += "a ctx_lens entry was outside [0, max_seq); its outputs are NaN. ";
     if (st[0] & 2) msg += "decode work items exceeded the workspace capacity. ";
     if (st[0] & 4) msg += "a bf16 input exceeded the fp16 operand range (|x| > 65504). ";
+    if (st[0] & 8) msg += "a bounded device wait ran out (attention pipeline aborted). ";
     return fail(ctx, B2A_EDEVICE, "%s", msg.c_str());
 }
 
@@ -364,7 +373,7 @@ B2A_API int b2a_mha(b2a_context* ctx, int in_dtype, int out_dtype, const void* q
         p.v = base + 2 * one;
         p.in_dtype = B2A_FLOAT16;
     }
-    e = attn_tc_supported(p) ? launch_attn_tc(p, s) : launch_attn_simt(p, s);
+    e = launch_attention(ctx, p, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "attention kernel launch");
     return B2A_OK;
 }
@@ -464,7 +473,7 @@ B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype, co
     }
     if (conv) p.v = v_c;
     p.in_dtype = cdt;
-    e = attn_tc_supported(p) ? launch_attn_tc(p, s) : launch_attn_simt(p, s);
+    e = launch_attention(ctx, p, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "attention kernel launch");
     return B2A_OK;
 }

@@ -1,0 +1,693 @@
+// attn_tcgen05.cu -- whole-sequence attention (causal prefill, bidirectional
+// encoder) on the 5th-generation tensor cores: tcgen05.mma with TMEM
+// accumulators, TMA-staged Q/K/V tiles, mbarrier pipeline.
+//
+// CTA = two tiles of 128 query rows (A and B) of one (batch, head), 320 threads:
+//   warps 0-3  softmax of tile A, warps 4-7 softmax of tile B: thread t of a
+//              group owns query row t = TMEM lane t (tcgen05.ld/st 32x32b);
+//   warp 8     TMA producer: Q_A, Q_B once, then K and V tiles of 128 keys
+//              into a 2-3 stage ring (plain tiled loads, 128-byte swizzle,
+//              64-element panels of the head dimension);
+//   warp 9     MMA issuer (one thread).  Per key tile j it issues
+//              O_A += P_A(j) V_j, S_A = Q_A K_{j+1}^T, O_B += P_B(j) V_j,
+//              S_B = Q_B K_{j+1}^T, so the tensor core works on one tile while
+//              the softmax group of the other runs (ping-pong).
+// TMEM (512 columns): S_A 0..127, S_B 128..255 (fp32 scores; the softmax
+// writes P as fp16 pairs over the first 64 columns, and the PV MMA reads it
+// from TMEM), O_A at 256, O_B at 384.
+// Softmax: two TMEM passes per tile (row max, then exp2 + row sum + P);
+// masks only on tiles that touch the causal diagonal, the window start or the
+// key end; the scale is folded into one FFMA per score; half of the exp2 run
+// on the FMA pipe as a degree-4 polynomial (see exp2_poly) to offload the
+// 16/clk/SM MUFU unit.  The running maximum moves lazily: O is rescaled only
+// when a row's maximum grows by more than 8 (log2 units), so P <= 2^8.
+//
+// Every mbarrier wait is bounded by %globaltimer (kWaitNs).  On a timeout the
+// kernel sets status bit 3; other roles stop at their next wait; the producer
+// waits (bounded) for its own TMA copies, the MMA thread drains its MMAs,
+// TMEM is freed and the CTA returns.
+//
+// Same semantics as attn_simt.cu / attn_mma.cu (the reference citations are
+// there); operands are fp16 (bf16 callers are converted by the host layer).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace b2a {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 128;
+constexpr int kThreadsTc = 320;
+constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s
+constexpr float kRescaleThreshold = 8.0f;
+constexpr uint32_t kTmemCols = 512;
+
+struct TcParams {
+    int B, S, Hq, Hkv, G, D;
+    int causal, window;
+    const float* mask;
+    const int32_t* key_len;
+    float scale;
+    float scale_log2;
+    void* out;
+    int out_dtype;
+    int64_t o_sb, o_ss, o_sh;
+    int* status;
+    int fmt;  // 0 = fp16, 1 = bf16 operands
+};
+
+template <int D>
+struct TcGeo {
+    static constexpr int NP = (D + 63) / 64;      // 128-byte panels per row
+    static constexpr int kPanelBytes = 128 * 128;  // 128 rows x 128 B
+    static constexpr int kTileBytes = NP * kPanelBytes;
+    static constexpr int kStages = D <= 64 ? 3 : 2;
+    static constexpr int oQ = 0;                   // Q_A, Q_B
+    static constexpr int oK = 2 * kTileBytes;
+    static constexpr int oV = oK + kStages * kTileBytes;
+    static constexpr int oBar = oV + kStages * kTileBytes;
+    static constexpr int kBytes = oBar + 512;
+    static constexpr uint32_t kTxKV = 2 * kTileBytes;
+    static_assert(kBytes + 1024 <= 227 * 1024, "shared memory budget");
+};
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// try_wait with a suspend-time hint: a waiting thread sleeps instead of spinning.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P1;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, P1;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(20000u)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false when kWaitNs elapse (status bit 3) or another role /
+// another CTA already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
+    if (mbar_test(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_test(bar, parity)) return true;
+        if ((i & 63u) == 0) {
+            if (*abort_flag) return false;
+            if (*(volatile int*)status & 8) {
+                *abort_flag = 1;
+                return false;
+            }
+            if (global_ns() - t0 > kWaitNs) {
+                *abort_flag = 1;
+                atomicOr(status, 8);
+                return false;
+            }
+        }
+    }
+}
+// Bounded wait on the exit path (no abort short-cut).
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = global_ns();
+    while (!mbar_test(bar, parity))
+        if (global_ns() - t0 > kWaitNs) return;
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, int c2,
+                                            int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(dst),
+        "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3));
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3));
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+#define B2A_R32(r) \
+    "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), \
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), \
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), \
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+
+// 32 consecutive 32-bit TMEM columns of this thread's lane (asynchronous until tmem_wait_ld).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : B2A_R32(r)
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+    tmem_st16(taddr, r);
+    tmem_st16(taddr + 16, r + 16);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm_100 version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor, kind::f16, fp32 accumulate.
+__host__ __device__ constexpr uint32_t make_idesc(int fmt, int M, int N, int a_mn_major, int b_mn_major) {
+    return (1u << 4) | ((uint32_t)fmt << 7) | ((uint32_t)fmt << 10) | ((uint32_t)a_mn_major << 15) |
+           ((uint32_t)b_mn_major << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// 2^x without the XU pipe (which the MUFU exp2 and the fp16 packing already
+// load): x = n + f with n = round(x) taken by adding 1.5 * 2^23 (the FP adder
+// rounds to an integer; n is then in the low mantissa bits), f in
+// [-0.5, 0.5]; 2^f by a degree-4 polynomial fitted here to 2^f on
+// [-0.5, 0.5] (least squares on Chebyshev nodes with relative-error
+// reweighting; max relative error 8.5e-6, far below the fp16 rounding of P);
+// 2^n added to the exponent field.  x is clamped at -126 so the exponent
+// stays non-negative: masked scores (-inf) give 2^-126, which is 0 in fp16.
+__device__ __forceinline__ float exp2_poly(float x) {
+    x = fmaxf(x, -126.f);
+    const float t = x + 12582912.f;                     // 1.5 * 2^23
+    const int ni = __float_as_int(t) - 0x4B400000;      // round(x) as an integer
+    const float f = x - (t - 12582912.f);
+    float p = fmaf(0.009254964f, f, 0.05585603f);
+    p = fmaf(p, f, 0.24031252f);
+    p = fmaf(p, f, 0.6931306f);
+    p = fmaf(p, f, 0.9999978f);
+    return __int_as_float(__float_as_int(p) + (ni << 23));
+}
+
+__device__ __forceinline__ void store8(void* out, int64_t off, const float* v, int dtype) {
+    if (dtype == kF32) {
+        float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + off);
+        o[0] = make_float4(v[0], v[1], v[2], v[3]);
+        o[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else if (dtype == kF16) {
+        uint4 u;
+        u.x = pack_half2(v[0], v[1]);
+        u.y = pack_half2(v[2], v[3]);
+        u.z = pack_half2(v[4], v[5]);
+        u.w = pack_half2(v[6], v[7]);
+        *reinterpret_cast<uint4*>(static_cast<__half*>(out) + off) = u;
+    } else {
+        uint4 u;
+        uint32_t* w = &u.x;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            w[i] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + off) = u;
+    }
+}
+
+// ---------------------------------------------------------------- kernel
+template <int D>
+__global__ void __launch_bounds__(kThreadsTc, 1)
+    attn_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcParams p) {
+    using Gm = TcGeo<D>;
+    constexpr int NP = Gm::NP;
+    constexpr int ST = Gm::kStages;
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    unsigned char* base_ptr = smem_raw + (base - smem_u32(smem_raw));
+    const uint32_t sQ = base + Gm::oQ, sK = base + Gm::oK, sV = base + Gm::oV;
+    const uint32_t bar0 = base + Gm::oBar;
+    // barriers, 8 bytes each
+    const uint32_t bQ = bar0;
+    auto bKVfull = [&](int s) { return bar0 + 8u * (1 + s); };
+    auto bKVempty = [&](int s) { return bar0 + 8u * (1 + ST + s); };
+    auto bSfull = [&](int t) { return bar0 + 8u * (1 + 2 * ST + t); };
+    auto bPfull = [&](int t) { return bar0 + 8u * (3 + 2 * ST + t); };
+    auto bOdone = [&](int t) { return bar0 + 8u * (5 + 2 * ST + t); };
+    const uint32_t bDrain = bar0 + 8u * (7 + 2 * ST);
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(base_ptr + Gm::oBar + 256);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(base_ptr + Gm::oBar + 264);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n_pairs = (p.S + 2 * kBM - 1) / (2 * kBM);
+    const int pair = p.causal ? n_pairs - 1 - (int)blockIdx.x : (int)blockIdx.x;
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int kvh = h / p.G;
+    const int qbase = pair * 2 * kBM;
+
+    // per query tile: first row, key range, number of key tiles
+    int q0t[2], kb[2], ke[2], nt[2];
+    bool uniform = false;
+    for (int t = 0; t < 2; ++t) {
+        q0t[t] = qbase + t * kBM;
+        kb[t] = 0;
+        ke[t] = p.S;
+        if (p.causal) {
+            ke[t] = min(p.S, q0t[t] + kBM);
+            if (p.window > 0) kb[t] = max(0, q0t[t] - p.window + 1);
+        } else if (p.key_len != nullptr) {
+            const int kl = p.key_len[b];
+            if (kl <= 0) uniform = true;
+            else ke[t] = min(kl, p.S);
+        }
+    }
+    const int t_begin = kb[0] / kBN;  // tile A starts no later than tile B
+    for (int t = 0; t < 2; ++t) nt[t] = q0t[t] < p.S ? (ke[t] + kBN - 1) / kBN - t_begin : 0;
+    const int n_max = max(nt[0], nt[1]);
+
+    if (tid == 0) {
+        mbar_init(bQ, 1);
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(bKVfull(s), 1);
+            mbar_init(bKVempty(s), 1);
+        }
+        for (int t = 0; t < 2; ++t) {
+            mbar_init(bSfull(t), 1);
+            mbar_init(bPfull(t), 128);
+            mbar_init(bOdone(t), 1);
+        }
+        mbar_init(bDrain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        __syncwarp();  // lane 0 ran the init branch alone; the allocation is warp-collective
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 8) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            int issued = 0;
+            mbar_expect_tx(bQ, 2 * Gm::kTileBytes);
+            for (int t = 0; t < 2; ++t)
+                for (int pn = 0; pn < NP; ++pn)
+                    tma_load_4d(sQ + t * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmQ, bQ, 64 * pn, h, q0t[t], b);
+            for (int j = 0; j < n_max; ++j) {
+                const int st = j % ST;
+                if (j >= ST && !mbar_wait(bKVempty(st), ((j / ST) - 1) & 1, abort_flag, p.status)) break;
+                const int n0 = (t_begin + j) * kBN;
+                mbar_expect_tx(bKVfull(st), Gm::kTxKV);
+                for (int pn = 0; pn < NP; ++pn) {
+                    tma_load_4d(sK + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmK, bKVfull(st), 64 * pn, kvh, n0,
+                                b);
+                    tma_load_4d(sV + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmV, bKVfull(st), 64 * pn, kvh, n0,
+                                b);
+                }
+                issued = j + 1;
+            }
+            // every copy this thread issued lands before the CTA may exit
+            mbar_drain(bQ, 0);
+            for (int j = (issued > ST ? issued - ST : 0); j < issued; ++j) mbar_drain(bKVfull(j % ST), (j / ST) & 1);
+        }
+    } else if (warp == 9) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idq = make_idesc(p.fmt, kBM, kBN, 0, 0);
+            const uint32_t idp = make_idesc(p.fmt, kBM, D, 0, 1);
+            int kv_ready = -1;  // highest key tile whose K/V wait was observed
+            bool ok = mbar_wait(bQ, 0, abort_flag, p.status);
+            auto wait_kv = [&](int j) -> bool {
+                if (kv_ready >= j) return true;
+                if (!mbar_wait(bKVfull(j % ST), (j / ST) & 1, abort_flag, p.status)) return false;
+                tc_fence_after();
+                kv_ready = j;
+                return true;
+            };
+            auto issue_qk = [&](int t, int j) {
+                const int st = j % ST;
+#pragma unroll
+                for (int ks = 0; ks < D / 16; ++ks) {
+                    const uint32_t koff = (uint32_t)(ks >> 2) * Gm::kPanelBytes + (uint32_t)(ks & 3) * 32u;
+                    const uint64_t da = smem_desc(sQ + t * Gm::kTileBytes + koff, 16, 1024);
+                    const uint64_t db = smem_desc(sK + st * Gm::kTileBytes + koff, 16, 1024);
+                    umma_ss(tmem + 128u * t, da, db, idq, ks > 0 ? 1u : 0u);
+                }
+                umma_commit(bSfull(t));
+            };
+            auto issue_pv = [&](int t, int j) {
+                const int st = j % ST;
+#pragma unroll
+                for (int kk = 0; kk < kBN / 16; ++kk) {
+                    // V tile, MN-major: 8-key atoms 1024 B apart (SBO), 64-column panels kPanelBytes apart (LBO)
+                    const uint64_t db = smem_desc(sV + st * Gm::kTileBytes + kk * 2048u, Gm::kPanelBytes, 1024);
+                    umma_ts(tmem + 256u + 128u * t, tmem + 128u * t + kk * 8u, db, idp, (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(bOdone(t));
+            };
+            if (ok && n_max > 0) {
+                ok = wait_kv(0);
+                for (int t = 0; t < 2 && ok; ++t)
+                    if (nt[t] > 0) issue_qk(t, 0);
+            }
+            for (int j = 0; j < n_max && ok; ++j) {
+                for (int t = 0; t < 2 && ok; ++t) {
+                    if (j >= nt[t]) continue;
+                    if (!mbar_wait(bPfull(t), j & 1, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_pv(t, j);
+                    if (j + 1 < nt[t]) {
+                        if (!wait_kv(j + 1)) {
+                            ok = false;
+                            break;
+                        }
+                        issue_qk(t, j + 1);
+                    }
+                }
+                umma_commit(bKVempty(j % ST));  // stage j is free once both PV(j) finish
+            }
+            // all MMAs this thread issued are complete before TMEM is released
+            umma_commit(bDrain);
+            mbar_drain(bDrain, 0);
+        }
+    } else {
+        // ------------------------------------------------------------ softmax groups
+        const int t = warp >> 2;       // 0: tile A, 1: tile B
+        const int row = tid & 127;     // TMEM lane within the group
+        // this group's tile bounds as scalars (no dynamically indexed arrays in the hot loop)
+        const int my_q0 = t ? q0t[1] : q0t[0];
+        const int my_kb = t ? kb[1] : kb[0];
+        const int my_ke = t ? ke[1] : ke[0];
+        const int my_nt = t ? nt[1] : nt[0];
+        const int q = my_q0 + row;
+        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const uint32_t s_addr = lane_base + (t ? 128u : 0u);
+        const uint32_t o_addr = lane_base + (t ? 384u : 256u);
+        const float sl2 = p.scale_log2;
+        const int q_lo = my_q0, q_hi = my_q0 + kBM - 1;
+        float m_run = -INFINITY, l_run = 0.f;
+        bool ok = true;
+        for (int j = 0; j < my_nt && ok; ++j) {
+            if (!__all_sync(0xffffffffu, mbar_wait(bSfull(t), j & 1, abort_flag, p.status))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int n0 = (t_begin + j) * kBN;
+            // a tile needs per-element masks when it touches the diagonal, the window start or the key end
+            const bool edge = uniform || p.mask != nullptr || n0 + kBN > my_ke || n0 < my_kb ||
+                              (p.causal && n0 + kBN - 1 > q_lo) ||
+                              (p.causal && p.window > 0 && n0 <= q_hi - p.window);
+            auto score = [&](float raw, int key) -> float {  // log2-domain score or -inf
+                bool vis = key < my_ke && key >= my_kb;
+                if (p.causal) vis = vis && key <= q && (p.window <= 0 || key > q - p.window);
+                if (!vis) return -INFINITY;
+                if (uniform) return 0.f;
+                if (p.mask != nullptr) return (raw * p.scale + p.mask[(int64_t)b * p.S + key]) * kLog2e;
+                return raw * sl2;
+            };
+            // pass 1: row maximum
+            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kBN / 32; c += 2) {
+                uint32_t r0[32], r1[32];
+                tmem_ld32(s_addr + 32 * c, r0);
+                tmem_ld32(s_addr + 32 * (c + 1), r1);
+                tmem_wait_ld();
+                if (edge) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) {
+                        mx0 = fmaxf(mx0, score(__uint_as_float(r0[i]), n0 + 32 * c + i));
+                        mx1 = fmaxf(mx1, score(__uint_as_float(r0[i + 1]), n0 + 32 * c + i + 1));
+                        mx2 = fmaxf(mx2, score(__uint_as_float(r1[i]), n0 + 32 * (c + 1) + i));
+                        mx3 = fmaxf(mx3, score(__uint_as_float(r1[i + 1]), n0 + 32 * (c + 1) + i + 1));
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 2) {
+                        mx0 = fmaxf(mx0, __uint_as_float(r0[i]));
+                        mx1 = fmaxf(mx1, __uint_as_float(r0[i + 1]));
+                        mx2 = fmaxf(mx2, __uint_as_float(r1[i]));
+                        mx3 = fmaxf(mx3, __uint_as_float(r1[i + 1]));
+                    }
+                }
+            }
+            float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+            if (!edge) mx *= sl2;
+            // lazy rescale: move the reference maximum only when it grew by > threshold
+            const bool need = mx > m_run + kRescaleThreshold;
+            if (__any_sync(0xffffffffu, need)) {
+                const float m_new = need ? mx : m_run;
+                const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
+                l_run *= alpha;
+                if (j > 0) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(bOdone(t), (j - 1) & 1, abort_flag, p.status))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int c = 0; c < D / 32; ++c) {
+                        uint32_t r[32];
+                        tmem_ld32(o_addr + 32 * c, r);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                        tmem_st32(o_addr + 32 * c, r);
+                    }
+                }
+                m_run = m_new;
+            }
+            const float mb = m_run == -INFINITY ? 0.f : m_run;
+            // pass 2: P = 2^(s - m), row sum, fp16 pairs over the consumed S columns
+            float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+            for (int c = 0; c < kBN / 32; c += 2) {
+                uint32_t r0[32], r1[32];
+                tmem_ld32(s_addr + 32 * c, r0);
+                tmem_ld32(s_addr + 32 * (c + 1), r1);
+                tmem_wait_ld();
+                // log2-domain arguments; the edge test stays outside the element loops so
+                // interior tiles run the one-FFMA path only
+                float x0[32], x1[32];
+                if (edge) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        x0[i] = score(__uint_as_float(r0[i]), n0 + 32 * c + i) - mb;
+                        x1[i] = score(__uint_as_float(r1[i]), n0 + 32 * (c + 1) + i) - mb;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        x0[i] = fmaf(__uint_as_float(r0[i]), sl2, -mb);
+                        x1[i] = fmaf(__uint_as_float(r1[i]), sl2, -mb);
+                    }
+                }
+                uint32_t pk0[16], pk1[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    // chunks 0-2 on the MUFU (8 cycles per warp instruction), chunk 3 on
+                    // the FMA pipe: 96 + 32 per row keeps both pipes under the MMA time
+                    const float e0 = fast_exp2(x0[i]), e1 = fast_exp2(x0[i + 1]);
+                    const float e2 = c == 0 ? fast_exp2(x1[i]) : exp2_poly(x1[i]);
+                    const float e3 = c == 0 ? fast_exp2(x1[i + 1]) : exp2_poly(x1[i + 1]);
+                    rs0 += e0 + e1;
+                    rs1 += e2 + e3;
+                    pk0[i / 2] = pack_half2(e0, e1);
+                    pk1[i / 2] = pack_half2(e2, e3);
+                }
+                tmem_st16(s_addr + 16 * c, pk0);
+                tmem_st16(s_addr + 16 * (c + 1), pk1);
+            }
+            l_run += rs0 + rs1;
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bPfull(t));
+        }
+        // epilogue: O / l for rows inside the sequence
+        if (ok && my_nt > 0 && __all_sync(0xffffffffu, mbar_wait(bOdone(t), (my_nt - 1) & 1, abort_flag, p.status))) {
+            tc_fence_after();
+            const float inv = 1.f / l_run;
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(o_addr + 32 * c, r);
+                tmem_wait_ld();
+                if (q < p.S) {
+                    const int64_t off = b * p.o_sb + (int64_t)q * p.o_ss + h * p.o_sh + 32 * c;
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        float v[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) v[k] = __uint_as_float(r[i + k]) * inv;
+                        store8(p.out, off + i, v, p.out_dtype);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+}
+
+// ---------------------------------------------------------------- host side
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+    static std::once_flag once;
+    static EncodeFn fn = nullptr;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeFn>(ptr);
+    });
+    return fn;
+}
+
+// [B][S][H][D] tensor (element strides sb, ss, sh; d contiguous), box 64 x 1 x 128 x 1.
+bool make_map(CUtensorMap* m, const void* ptr, int fmt, int B, int S, int H, int D, int64_t sb, int64_t ss,
+              int64_t sh) {
+    EncodeFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+    const cuuint64_t strides[3] = {(cuuint64_t)sh * 2, (cuuint64_t)ss * 2, (cuuint64_t)sb * 2};
+    const cuuint32_t box[4] = {64, 1, 128, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = fn(m, fmt ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                          const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int D>
+cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream) {
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    // at least 116 KB so no two CTAs share an SM: each one allocates all 512 TMEM columns
+    const int smem = TcGeo<D>::kBytes + 1024 > 116 * 1024 ? TcGeo<D>::kBytes + 1024 : 116 * 1024;
+    std::call_once(once, [&] {
+        attr_err = cudaFuncSetAttribute(attn_tcgen05_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    });
+    if (attr_err != cudaSuccess) return attr_err;
+    const int fmt = a.in_dtype == kBF16 ? 1 : 0;
+    CUtensorMap mq, mk, mv;
+    if (!make_map(&mq, a.q, fmt, a.B, a.S, a.Hq, a.D, a.q_sb, a.q_ss, a.q_sh) ||
+        !make_map(&mk, a.k, fmt, a.B, a.S, a.Hkv, a.D, a.k_sb, a.k_ss, a.k_sh) ||
+        !make_map(&mv, a.v, fmt, a.B, a.S, a.Hkv, a.D, a.k_sb, a.k_ss, a.k_sh))
+        return cudaErrorInvalidValue;
+    TcParams p{};
+    p.B = a.B;
+    p.S = a.S;
+    p.Hq = a.Hq;
+    p.Hkv = a.Hkv;
+    p.G = a.Hq / a.Hkv;
+    p.D = a.D;
+    p.causal = a.causal;
+    p.window = a.window;
+    p.mask = a.mask;
+    p.key_len = a.key_len;
+    p.scale = a.scale;
+    p.scale_log2 = a.scale * kLog2e;
+    p.out = a.o;
+    p.out_dtype = a.out_dtype;
+    p.o_sb = a.q_sb;
+    p.o_ss = a.q_ss;
+    p.o_sh = a.q_sh;
+    p.status = status;
+    p.fmt = fmt;
+    dim3 grid((a.S + 2 * kBM - 1) / (2 * kBM), a.Hq, a.B);
+    attn_tcgen05_kernel<D><<<grid, kThreadsTc, smem, stream>>>(mq, mk, mv, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool attn_tcgen05_supported(const AttnParams& p) {
+    if (p.in_dtype != kF16 && p.in_dtype != kBF16) return false;
+    if (!(p.D == 64 || p.D == 96 || p.D == 128)) return false;
+    const int64_t strides[] = {p.q_sb, p.q_ss, p.q_sh, p.k_sb, p.k_ss, p.k_sh};
+    for (int64_t s : strides)
+        if (s % 8 != 0 || s <= 0) return false;
+    const uintptr_t ptrs[] = {(uintptr_t)p.q, (uintptr_t)p.k, (uintptr_t)p.v, (uintptr_t)p.o};
+    for (uintptr_t x : ptrs)
+        if (x % 16 != 0) return false;
+    return p.Hq <= 65535 && p.B <= 65535 && encode_fn() != nullptr;
+}
+
+cudaError_t launch_attn_tcgen05(const AttnParams& p, int* status, cudaStream_t stream) {
+    switch (p.D) {
+        case 64: return launch_impl<64>(p, status, stream);
+        case 96: return launch_impl<96>(p, status, stream);
+        case 128: return launch_impl<128>(p, status, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace b2a
