@@ -44,9 +44,22 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBN = 128;
-constexpr int kThreadsTc = 320;
+constexpr int kThreadsTc = 384;
+// Register split between the warpgroups (setmaxnreg): the kernel launches with
+// kRegsLaunch per thread (ptxas' limit for 384 threads and one CTA per SM, which
+// the host checks before launching); the control warpgroup returns registers so
+// the two softmax warpgroups can keep a whole 128-column score row resident.
+// 2 * kRegsSoftmax + kRegsControl == 3 * kRegsLaunch: the pool is used exactly.
+constexpr int kRegsLaunch = 168;
+constexpr int kRegsSoftmax = 224;
+constexpr int kRegsControl = 56;
+static_assert(2 * kRegsSoftmax + kRegsControl == 3 * kRegsLaunch, "register split must equal the launch pool");
 constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s
 constexpr float kRescaleThreshold = 8.0f;
+#ifndef B2A_POLY_PAIRS
+#define B2A_POLY_PAIRS 2
+#endif
+constexpr int kPolyPairs = B2A_POLY_PAIRS;  // of every 8 exp2 pairs, on the FMA pipe
 constexpr uint32_t kTmemCols = 512;
 
 struct TcParams {
@@ -93,15 +106,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
-// try_wait with a suspend-time hint: a waiting thread sleeps instead of spinning.
+// try_wait without a suspend-time hint: the thread retries at the hardware's
+// own short interval.
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred P1;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2, %3;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
         "selp.b32 %0, 1, 0, P1;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(20000u)
+        : "r"(bar), "r"(parity)
         : "memory");
     return ok != 0;
 }
@@ -112,7 +126,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     const uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_test(bar, parity)) return true;
-        if ((i & 63u) == 0) {
+        if ((i & 1023u) == 0) {
             if (*abort_flag) return false;
             if (*(volatile int*)status & 8) {
                 *abort_flag = 1;
@@ -168,6 +182,43 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                  : "memory");
+}
+// Warp-wide forms of the three: the whole warp computes the (warp-uniform)
+// operands and lane 0 alone issues, so the descriptors stay in the uniform
+// datapath instead of being moved there for every instruction.
+// Descriptors travel as two 32-bit words: only the low word (start address and
+// LBO fields) changes between K steps, tiles and stages; the high word (SBO,
+// version, layout) is one constant per operand.
+template <int kAcc>  // 0: overwrite, 1: accumulate, -1: the runtime flag `acc`
+__device__ __forceinline__ void umma_ss_w(uint32_t lane, uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                          uint32_t b_hi, uint32_t idesc, uint32_t acc = 0) {
+    asm volatile(
+        "{\n\t.reg .pred p, l0;\n\t.reg .b64 da, db;\n\t"
+        "setp.eq.u32 l0, %7, 0;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "mov.b64 da, {%1, %2};\n\t"
+        "mov.b64 db, {%3, %4};\n\t"
+        "@l0 tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(kAcc < 0 ? acc : (uint32_t)kAcc), "r"(lane));
+}
+template <int kAcc>
+__device__ __forceinline__ void umma_ts_w(uint32_t lane, uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo,
+                                          uint32_t b_hi, uint32_t idesc, uint32_t acc = 0) {
+    asm volatile(
+        "{\n\t.reg .pred p, l0;\n\t.reg .b64 db;\n\t"
+        "setp.eq.u32 l0, %6, 0;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "mov.b64 db, {%2, %3};\n\t"
+        "@l0 tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(kAcc < 0 ? acc : (uint32_t)kAcc), "r"(lane));
+}
+__device__ __forceinline__ void umma_commit_w(uint32_t lane, uint32_t bar) {
+    asm volatile(
+        "{\n\t.reg .pred l0;\n\t"
+        "setp.eq.u32 l0, %1, 0;\n\t"
+        "@l0 tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar),
+        "r"(lane)
+        : "memory");
 }
 
 #define B2A_R32(r) \
@@ -241,6 +292,50 @@ __device__ __forceinline__ float exp2_poly(float x) {
     return __int_as_float(__float_as_int(p) + (ni << 23));
 }
 
+// Pairs of fp32 in one 64-bit register: the f32x2 instructions of sm_100 do two
+// lanes per issue slot on the FMA pipe.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 f2_make(float lo, float hi) {
+    f32x2 d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ void f2_split(f32x2 v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f32x2 f2_fma(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ f32x2 f2_add(f32x2 a, f32x2 b) {
+    f32x2 d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+// exp2_poly on a pair: the same operations, rounding and polynomial, two lanes
+// per f32x2 instruction.
+__device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& e0, float& e1) {
+    const f32x2 x = f2_make(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+    const f32x2 t = f2_add(x, f2_make(12582912.f, 12582912.f));
+    const f32x2 f = f2_fma(f2_add(t, f2_make(-12582912.f, -12582912.f)), f2_make(-1.f, -1.f), x);  // x - round(x)
+    f32x2 p = f2_fma(f2_make(0.009254964f, 0.009254964f), f, f2_make(0.05585603f, 0.05585603f));
+    p = f2_fma(p, f, f2_make(0.24031252f, 0.24031252f));
+    p = f2_fma(p, f, f2_make(0.6931306f, 0.6931306f));
+    p = f2_fma(p, f, f2_make(0.9999978f, 0.9999978f));
+    float p0, p1, t0, t1;
+    f2_split(p, p0, p1);
+    f2_split(t, t0, t1);
+    // the low mantissa bits of t hold round(x); shifted by 23 they land in the exponent
+    e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+    e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
 __device__ __forceinline__ void store8(void* out, int64_t off, const float* v, int dtype) {
     if (dtype == kF32) {
         float4* o = reinterpret_cast<float4*>(static_cast<float*>(out) + off);
@@ -266,7 +361,9 @@ __device__ __forceinline__ void store8(void* out, int64_t off, const float* v, i
 }
 
 // ---------------------------------------------------------------- kernel
-template <int D>
+// kAdditive: the additive [B][S] key mask is applied (its own instantiation, so the
+// mask loads do not weigh on the register budget of the unmasked kernels).
+template <int D, bool kAdditive>
 __global__ void __launch_bounds__(kThreadsTc, 1)
     attn_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ TcParams p) {
@@ -290,8 +387,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(base_ptr + Gm::oBar + 264);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n_pairs = (p.S + 2 * kBM - 1) / (2 * kBM);
-    const int pair = p.causal ? n_pairs - 1 - (int)blockIdx.x : (int)blockIdx.x;
+    // parameter fields copied to registers once: the asm statements below clobber
+    // memory, which would otherwise force a reload through a generic pointer at
+    // every use (a 25x slower masked softmax tile when the mask test read them)
+    const int S = p.S, causal = p.causal, window = p.window;
+    const float* const mask = kAdditive ? p.mask : nullptr;
+    const float scale = p.scale;
+    int* const status = p.status;
+    const int n_pairs = (S + 2 * kBM - 1) / (2 * kBM);
+    const int pair = causal ? n_pairs - 1 - (int)blockIdx.x : (int)blockIdx.x;
     const int h = blockIdx.y, b = blockIdx.z;
     const int kvh = h / p.G;
     const int qbase = pair * 2 * kBM;
@@ -302,18 +406,18 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     for (int t = 0; t < 2; ++t) {
         q0t[t] = qbase + t * kBM;
         kb[t] = 0;
-        ke[t] = p.S;
-        if (p.causal) {
-            ke[t] = min(p.S, q0t[t] + kBM);
-            if (p.window > 0) kb[t] = max(0, q0t[t] - p.window + 1);
+        ke[t] = S;
+        if (causal) {
+            ke[t] = min(S, q0t[t] + kBM);
+            if (window > 0) kb[t] = max(0, q0t[t] - window + 1);
         } else if (p.key_len != nullptr) {
             const int kl = p.key_len[b];
             if (kl <= 0) uniform = true;
-            else ke[t] = min(kl, p.S);
+            else ke[t] = min(kl, S);
         }
     }
     const int t_begin = kb[0] / kBN;  // tile A starts no later than tile B
-    for (int t = 0; t < 2; ++t) nt[t] = q0t[t] < p.S ? (ke[t] + kBN - 1) / kBN - t_begin : 0;
+    for (int t = 0; t < 2; ++t) nt[t] = q0t[t] < S ? (ke[t] + kBN - 1) / kBN - t_begin : 0;
     const int n_max = max(nt[0], nt[1]);
 
     if (tid == 0) {
@@ -342,7 +446,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
-    if (warp == 8) {
+    if (warp >= 8) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+      if (warp == 8) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             int issued = 0;
@@ -352,7 +458,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                     tma_load_4d(sQ + t * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmQ, bQ, 64 * pn, h, q0t[t], b);
             for (int j = 0; j < n_max; ++j) {
                 const int st = j % ST;
-                if (j >= ST && !mbar_wait(bKVempty(st), ((j / ST) - 1) & 1, abort_flag, p.status)) break;
+                if (j >= ST && !mbar_wait(bKVempty(st), ((j / ST) - 1) & 1, abort_flag, status)) break;
                 const int n0 = (t_begin + j) * kBN;
                 mbar_expect_tx(bKVfull(st), Gm::kTxKV);
                 for (int pn = 0; pn < NP; ++pn) {
@@ -369,38 +475,48 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         }
     } else if (warp == 9) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        // The whole warp runs this loop with warp-uniform waits (vote.all); lane 0
+        // issues the MMAs and commits.
+        {
+            const uint32_t ln = (uint32_t)lane;
             const uint32_t idq = make_idesc(p.fmt, kBM, kBN, 0, 0);
             const uint32_t idp = make_idesc(p.fmt, kBM, D, 0, 1);
             int kv_ready = -1;  // highest key tile whose K/V wait was observed
-            bool ok = mbar_wait(bQ, 0, abort_flag, p.status);
+            bool ok = __all_sync(0xffffffffu, mbar_wait(bQ, 0, abort_flag, status));
             auto wait_kv = [&](int j) -> bool {
                 if (kv_ready >= j) return true;
-                if (!mbar_wait(bKVfull(j % ST), (j / ST) & 1, abort_flag, p.status)) return false;
+                if (!__all_sync(0xffffffffu, mbar_wait(bKVfull(j % ST), (j / ST) & 1, abort_flag, status)))
+                    return false;
                 tc_fence_after();
                 kv_ready = j;
                 return true;
             };
+            // descriptors of each buffer's start: a K step, tile or stage offset only moves the
+            // 14-bit start-address field (addr >> 4) of the low word, and every offset here stays inside it
+            const uint64_t dQ = smem_desc(sQ, 16, 1024), dK = smem_desc(sK, 16, 1024);
+            const uint64_t dV = smem_desc(sV, Gm::kPanelBytes, 1024);
+            const uint32_t q_lo = (uint32_t)dQ, k_lo = (uint32_t)dK, v_lo = (uint32_t)dV;
+            const uint32_t qk_hi = (uint32_t)(dQ >> 32), v_hi = (uint32_t)(dV >> 32);  // dK's high word is dQ's
             auto issue_qk = [&](int t, int j) {
-                const int st = j % ST;
+                const uint32_t a0 = q_lo + (uint32_t)(t * Gm::kTileBytes >> 4);
+                const uint32_t b0 = k_lo + (uint32_t)((j % ST) * Gm::kTileBytes >> 4);
+                const uint32_t d = tmem + 128u * t;
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ++ks) {
-                    const uint32_t koff = (uint32_t)(ks >> 2) * Gm::kPanelBytes + (uint32_t)(ks & 3) * 32u;
-                    const uint64_t da = smem_desc(sQ + t * Gm::kTileBytes + koff, 16, 1024);
-                    const uint64_t db = smem_desc(sK + st * Gm::kTileBytes + koff, 16, 1024);
-                    umma_ss(tmem + 128u * t, da, db, idq, ks > 0 ? 1u : 0u);
+                    const uint32_t koff = ((uint32_t)(ks >> 2) * Gm::kPanelBytes + (uint32_t)(ks & 3) * 32u) >> 4;
+                    if (ks == 0) umma_ss_w<0>(ln, d, a0, qk_hi, b0, qk_hi, idq);
+                    else umma_ss_w<1>(ln, d, a0 + koff, qk_hi, b0 + koff, qk_hi, idq);
                 }
-                umma_commit(bSfull(t));
+                umma_commit_w(ln, bSfull(t));
             };
             auto issue_pv = [&](int t, int j) {
-                const int st = j % ST;
+                // V tile, MN-major: 8-key atoms 1024 B apart (SBO), 64-column panels kPanelBytes apart (LBO)
+                const uint32_t b0 = v_lo + (uint32_t)((j % ST) * Gm::kTileBytes >> 4);
+                const uint32_t d = tmem + 256u + 128u * t, a = tmem + 128u * t;
+                umma_ts_w<-1>(ln, d, a, b0, v_hi, idp, j > 0 ? 1u : 0u);
 #pragma unroll
-                for (int kk = 0; kk < kBN / 16; ++kk) {
-                    // V tile, MN-major: 8-key atoms 1024 B apart (SBO), 64-column panels kPanelBytes apart (LBO)
-                    const uint64_t db = smem_desc(sV + st * Gm::kTileBytes + kk * 2048u, Gm::kPanelBytes, 1024);
-                    umma_ts(tmem + 256u + 128u * t, tmem + 128u * t + kk * 8u, db, idp, (j > 0 || kk > 0) ? 1u : 0u);
-                }
-                umma_commit(bOdone(t));
+                for (int kk = 1; kk < kBN / 16; ++kk) umma_ts_w<1>(ln, d, a + kk * 8u, b0 + kk * 128u, v_hi, idp);
+                umma_commit_w(ln, bOdone(t));
             };
             if (ok && n_max > 0) {
                 ok = wait_kv(0);
@@ -408,9 +524,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                     if (nt[t] > 0) issue_qk(t, 0);
             }
             for (int j = 0; j < n_max && ok; ++j) {
+                // rolled over the two tiles: unrolled, each tile's per-step descriptor words
+                // would be loop-invariant and hoisted into (spilled) registers
+#pragma unroll 1
                 for (int t = 0; t < 2 && ok; ++t) {
                     if (j >= nt[t]) continue;
-                    if (!mbar_wait(bPfull(t), j & 1, abort_flag, p.status)) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(bPfull(t), j & 1, abort_flag, status))) {
                         ok = false;
                         break;
                     }
@@ -424,13 +543,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                         issue_qk(t, j + 1);
                     }
                 }
-                umma_commit(bKVempty(j % ST));  // stage j is free once both PV(j) finish
+                umma_commit_w(ln, bKVempty(j % ST));  // stage j is free once both PV(j) finish
             }
-            // all MMAs this thread issued are complete before TMEM is released
-            umma_commit(bDrain);
+            // all MMAs lane 0 issued are complete before TMEM is released
+            umma_commit_w(ln, bDrain);
             mbar_drain(bDrain, 0);
         }
+      }
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
         // ------------------------------------------------------------ softmax groups
         const int t = warp >> 2;       // 0: tile A, 1: tile B
         const int row = tid & 127;     // TMEM lane within the group
@@ -445,52 +566,55 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         const uint32_t o_addr = lane_base + (t ? 384u : 256u);
         const float sl2 = p.scale_log2;
         const int q_lo = my_q0, q_hi = my_q0 + kBM - 1;
+        // keys this row sees: [row_lo, row_hi); a uniform row (no valid key) weights all keys equally
+        int row_lo = my_kb, row_hi = my_ke;
+        if (causal) {
+            row_hi = min(row_hi, q + 1);
+            if (window > 0) row_lo = max(row_lo, q - window + 1);
+        }
+        const float edge_mult = uniform ? 0.f : sl2;
+        const bool additive = kAdditive && !uniform;
         float m_run = -INFINITY, l_run = 0.f;
         bool ok = true;
         for (int j = 0; j < my_nt && ok; ++j) {
-            if (!__all_sync(0xffffffffu, mbar_wait(bSfull(t), j & 1, abort_flag, p.status))) {
+            if (!__all_sync(0xffffffffu, mbar_wait(bSfull(t), j & 1, abort_flag, status))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const int n0 = (t_begin + j) * kBN;
             // a tile needs per-element masks when it touches the diagonal, the window start or the key end
-            const bool edge = uniform || p.mask != nullptr || n0 + kBN > my_ke || n0 < my_kb ||
-                              (p.causal && n0 + kBN - 1 > q_lo) ||
-                              (p.causal && p.window > 0 && n0 <= q_hi - p.window);
-            auto score = [&](float raw, int key) -> float {  // log2-domain score or -inf
-                bool vis = key < my_ke && key >= my_kb;
-                if (p.causal) vis = vis && key <= q && (p.window <= 0 || key > q - p.window);
-                if (!vis) return -INFINITY;
-                if (uniform) return 0.f;
-                if (p.mask != nullptr) return (raw * p.scale + p.mask[(int64_t)b * p.S + key]) * kLog2e;
-                return raw * sl2;
-            };
-            // pass 1: row maximum
-            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+            const bool edge = uniform || kAdditive || n0 + kBN > my_ke || n0 < my_kb ||
+                              (causal && n0 + kBN - 1 > q_lo) || (causal && window > 0 && n0 <= q_hi - window);
+            // the whole score row in registers: one TMEM read serves both passes
+            uint32_t r[kBN];
 #pragma unroll
-            for (int c = 0; c < kBN / 32; c += 2) {
-                uint32_t r0[32], r1[32];
-                tmem_ld32(s_addr + 32 * c, r0);
-                tmem_ld32(s_addr + 32 * (c + 1), r1);
-                tmem_wait_ld();
-                if (edge) {
+            for (int c = 0; c < kBN / 32; ++c) tmem_ld32(s_addr + 32 * c, r + 32 * c);
+            tmem_wait_ld();
+            if (edge) {
+                // masked tiles become log2-domain scores (-inf outside the row's keys)
+                const int lo = row_lo - n0, hi = row_hi - n0;
+                if (additive) {
+                    const float* mrow = mask + (int64_t)b * S + n0;
 #pragma unroll
-                    for (int i = 0; i < 32; i += 2) {
-                        mx0 = fmaxf(mx0, score(__uint_as_float(r0[i]), n0 + 32 * c + i));
-                        mx1 = fmaxf(mx1, score(__uint_as_float(r0[i + 1]), n0 + 32 * c + i + 1));
-                        mx2 = fmaxf(mx2, score(__uint_as_float(r1[i]), n0 + 32 * (c + 1) + i));
-                        mx3 = fmaxf(mx3, score(__uint_as_float(r1[i + 1]), n0 + 32 * (c + 1) + i + 1));
-                    }
+                    for (int i = 0; i < kBN; ++i)
+                        r[i] = __float_as_uint(i >= lo && i < hi
+                                                   ? (__uint_as_float(r[i]) * scale + __ldg(mrow + i)) * kLog2e
+                                                   : -INFINITY);
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 32; i += 2) {
-                        mx0 = fmaxf(mx0, __uint_as_float(r0[i]));
-                        mx1 = fmaxf(mx1, __uint_as_float(r0[i + 1]));
-                        mx2 = fmaxf(mx2, __uint_as_float(r1[i]));
-                        mx3 = fmaxf(mx3, __uint_as_float(r1[i + 1]));
-                    }
+                    for (int i = 0; i < kBN; ++i)
+                        r[i] = __float_as_uint(i >= lo && i < hi ? __uint_as_float(r[i]) * edge_mult : -INFINITY);
                 }
+            }
+            // pass 1: row maximum (raw scores on interior tiles, scaled after)
+            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < kBN; i += 8) {
+                mx0 = max3f(mx0, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+                mx1 = max3f(mx1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+                mx2 = max3f(mx2, __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+                mx3 = max3f(mx3, __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
             }
             float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
             if (!edge) mx *= sl2;
@@ -501,71 +625,55 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
                 l_run *= alpha;
                 if (j > 0) {
-                    if (!__all_sync(0xffffffffu, mbar_wait(bOdone(t), (j - 1) & 1, abort_flag, p.status))) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(bOdone(t), (j - 1) & 1, abort_flag, status))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
 #pragma unroll
                     for (int c = 0; c < D / 32; ++c) {
-                        uint32_t r[32];
-                        tmem_ld32(o_addr + 32 * c, r);
+                        uint32_t o[32];
+                        tmem_ld32(o_addr + 32 * c, o);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                        tmem_st32(o_addr + 32 * c, r);
+                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st32(o_addr + 32 * c, o);
                     }
                 }
                 m_run = m_new;
             }
             const float mb = m_run == -INFINITY ? 0.f : m_run;
-            // pass 2: P = 2^(s - m), row sum, fp16 pairs over the consumed S columns
-            float rs0 = 0.f, rs1 = 0.f;
+            // pass 2: P = 2^(s - m) as fp16 pairs over the first 64 S columns, row sum
+            const float mul = edge ? 1.f : sl2;
+            const f32x2 mul2 = f2_make(mul, mul), nmb2 = f2_make(-mb, -mb);
+            f32x2 sum0 = 0ull, sum1 = 0ull;
+            uint32_t pk[kBN / 2];
 #pragma unroll
-            for (int c = 0; c < kBN / 32; c += 2) {
-                uint32_t r0[32], r1[32];
-                tmem_ld32(s_addr + 32 * c, r0);
-                tmem_ld32(s_addr + 32 * (c + 1), r1);
-                tmem_wait_ld();
-                // log2-domain arguments; the edge test stays outside the element loops so
-                // interior tiles run the one-FFMA path only
-                float x0[32], x1[32];
-                if (edge) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        x0[i] = score(__uint_as_float(r0[i]), n0 + 32 * c + i) - mb;
-                        x1[i] = score(__uint_as_float(r1[i]), n0 + 32 * (c + 1) + i) - mb;
-                    }
+            for (int i = 0; i < kBN; i += 2) {
+                float x0, x1, e0, e1;
+                f2_split(f2_fma(f2_make(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), mul2, nmb2), x0, x1);
+                // kPolyPairs of every 8 pairs on the FMA pipe, the rest on the MUFU
+                if (((i >> 1) & 7) >= 8 - kPolyPairs) {
+                    exp2_poly_pair(x0, x1, e0, e1);
                 } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        x0[i] = fmaf(__uint_as_float(r0[i]), sl2, -mb);
-                        x1[i] = fmaf(__uint_as_float(r1[i]), sl2, -mb);
-                    }
+                    e0 = fast_exp2(x0);
+                    e1 = fast_exp2(x1);
                 }
-                uint32_t pk0[16], pk1[16];
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    // chunks 0-2 on the MUFU (8 cycles per warp instruction), chunk 3 on
-                    // the FMA pipe: 96 + 32 per row keeps both pipes under the MMA time
-                    const float e0 = fast_exp2(x0[i]), e1 = fast_exp2(x0[i + 1]);
-                    const float e2 = c == 0 ? fast_exp2(x1[i]) : exp2_poly(x1[i]);
-                    const float e3 = c == 0 ? fast_exp2(x1[i + 1]) : exp2_poly(x1[i + 1]);
-                    rs0 += e0 + e1;
-                    rs1 += e2 + e3;
-                    pk0[i / 2] = pack_half2(e0, e1);
-                    pk1[i / 2] = pack_half2(e2, e3);
-                }
-                tmem_st16(s_addr + 16 * c, pk0);
-                tmem_st16(s_addr + 16 * (c + 1), pk1);
+                if ((i >> 1) & 1) sum1 = f2_add(sum1, f2_make(e0, e1));
+                else sum0 = f2_add(sum0, f2_make(e0, e1));
+                pk[i >> 1] = pack_half2(e0, e1);
+                if (((i >> 1) & 15) == 15) tmem_st16(s_addr + (uint32_t)((i >> 1) - 15), pk + (i >> 1) - 15);
             }
-            l_run += rs0 + rs1;
+            float a0, a1, b0, b1;
+            f2_split(sum0, a0, a1);
+            f2_split(sum1, b0, b1);
+            l_run += (a0 + a1) + (b0 + b1);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bPfull(t));
         }
         // epilogue: O / l for rows inside the sequence
-        if (ok && my_nt > 0 && __all_sync(0xffffffffu, mbar_wait(bOdone(t), (my_nt - 1) & 1, abort_flag, p.status))) {
+        if (ok && my_nt > 0 && __all_sync(0xffffffffu, mbar_wait(bOdone(t), (my_nt - 1) & 1, abort_flag, status))) {
             tc_fence_after();
             const float inv = 1.f / l_run;
 #pragma unroll
@@ -573,7 +681,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 uint32_t r[32];
                 tmem_ld32(o_addr + 32 * c, r);
                 tmem_wait_ld();
-                if (q < p.S) {
+                if (q < S) {
                     const int64_t off = b * p.o_sb + (int64_t)q * p.o_ss + h * p.o_sh + 32 * c;
 #pragma unroll
                     for (int i = 0; i < 32; i += 8) {
@@ -627,16 +735,45 @@ bool make_map(CUtensorMap* m, const void* ptr, int fmt, int B, int S, int H, int
 }
 
 template <int D>
-cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream) {
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
+constexpr int smem_request() {
     // at least 116 KB so no two CTAs share an SM: each one allocates all 512 TMEM columns
-    const int smem = TcGeo<D>::kBytes + 1024 > 116 * 1024 ? TcGeo<D>::kBytes + 1024 : 116 * 1024;
-    std::call_once(once, [&] {
-        attr_err = cudaFuncSetAttribute(attn_tcgen05_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    return TcGeo<D>::kBytes + 1024 > 116 * 1024 ? TcGeo<D>::kBytes + 1024 : 116 * 1024;
+}
+
+// One-time setup of an instantiation on the current device: the shared-memory
+// opt-in, and the check that ptxas gave it exactly kRegsLaunch registers per
+// thread, the pool the setmaxnreg split in the kernel divides (with any other
+// count the softmax warpgroups' increase could not be met, so the kernel is
+// reported unsupported and the caller takes another path).
+constexpr int kMaxDevices = 64;
+template <int D, bool kAdditive>
+cudaError_t kernel_ready() {
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t err[kMaxDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::call_once(once[dev], [dev] {
+        cudaFuncAttributes fa{};
+        cudaError_t e = cudaFuncGetAttributes(&fa, attn_tcgen05_kernel<D, kAdditive>);
+        if (e == cudaSuccess && fa.numRegs != kRegsLaunch) e = cudaErrorInvalidDeviceFunction;
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(attn_tcgen05_kernel<D, kAdditive>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     smem_request<D>());
+        err[dev] = e;
     });
-    if (attr_err != cudaSuccess) return attr_err;
-    const int fmt = a.in_dtype == kBF16 ? 1 : 0;
+    return err[dev];
+}
+template <int D>
+cudaError_t kernel_ready_for(const AttnParams& p) {
+    return p.mask != nullptr ? kernel_ready<D, true>() : kernel_ready<D, false>();
+}
+
+template <int D>
+cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream) {
+    const bool additive = a.mask != nullptr;
+    const cudaError_t ready = kernel_ready_for<D>(a);
+    if (ready != cudaSuccess) return ready;
+    const int fmt = 0;  // fp16 operands (attn_tcgen05_supported)
     CUtensorMap mq, mk, mv;
     if (!make_map(&mq, a.q, fmt, a.B, a.S, a.Hq, a.D, a.q_sb, a.q_ss, a.q_sh) ||
         !make_map(&mk, a.k, fmt, a.B, a.S, a.Hkv, a.D, a.k_sb, a.k_ss, a.k_sh) ||
@@ -663,14 +800,18 @@ cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream) {
     p.status = status;
     p.fmt = fmt;
     dim3 grid((a.S + 2 * kBM - 1) / (2 * kBM), a.Hq, a.B);
-    attn_tcgen05_kernel<D><<<grid, kThreadsTc, smem, stream>>>(mq, mk, mv, p);
+    if (additive)
+        attn_tcgen05_kernel<D, true><<<grid, kThreadsTc, smem_request<D>(), stream>>>(mq, mk, mv, p);
+    else
+        attn_tcgen05_kernel<D, false><<<grid, kThreadsTc, smem_request<D>(), stream>>>(mq, mk, mv, p);
     return cudaGetLastError();
 }
 
 }  // namespace
 
 bool attn_tcgen05_supported(const AttnParams& p) {
-    if (p.in_dtype != kF16 && p.in_dtype != kBF16) return false;
+    // fp16 operands only: P goes to TMEM as fp16 and both MMA operands share one type
+    if (p.in_dtype != kF16) return false;
     if (!(p.D == 64 || p.D == 96 || p.D == 128)) return false;
     const int64_t strides[] = {p.q_sb, p.q_ss, p.q_sh, p.k_sb, p.k_ss, p.k_sh};
     for (int64_t s : strides)
@@ -678,7 +819,10 @@ bool attn_tcgen05_supported(const AttnParams& p) {
     const uintptr_t ptrs[] = {(uintptr_t)p.q, (uintptr_t)p.k, (uintptr_t)p.v, (uintptr_t)p.o};
     for (uintptr_t x : ptrs)
         if (x % 16 != 0) return false;
-    return p.Hq <= 65535 && p.B <= 65535 && encode_fn() != nullptr;
+    if (p.Hq > 65535 || p.B > 65535 || encode_fn() == nullptr) return false;
+    const cudaError_t ready = p.D == 64 ? kernel_ready_for<64>(p) : p.D == 96 ? kernel_ready_for<96>(p)
+                                                                               : kernel_ready_for<128>(p);
+    return ready == cudaSuccess;
 }
 
 cudaError_t launch_attn_tcgen05(const AttnParams& p, int* status, cudaStream_t stream) {

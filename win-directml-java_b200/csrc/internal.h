@@ -80,7 +80,7 @@ struct AttnParams {
 };
 
 cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t stream);
-// tcgen05 / TMEM / TMA kernel (fp16 or bf16, head_dim 64, 96, 128); status bit 3 = bounded wait ran out.
+// tcgen05 / TMEM / TMA kernel (fp16 operands, head_dim 64, 96, 128); status bit 3 = bounded wait ran out.
 bool attn_tcgen05_supported(const AttnParams& p);
 cudaError_t launch_attn_tcgen05(const AttnParams& p, int* status, cudaStream_t stream);
 bool attn_tc_supported(const AttnParams& p);
