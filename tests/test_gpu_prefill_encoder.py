@@ -159,3 +159,51 @@ def test_encoder_additive_mask_fp16(ctx):
                  mask=torch.from_numpy(mask).cuda())
     torch.cuda.synchronize()
     assert_close(to_np(y), want, what="additive mask")
+
+
+def _rotate_rows(x, *, B, S, H, D, pos0, theta, mode):
+    """The oracle's rotation of every [b, s] row block at position pos0 + s."""
+    fn = oracle.rope_half_gemma if mode == "gemma" else oracle.rope_decoderonly
+    out = np.empty_like(x)
+    for b in range(B):
+        for s in range(S):
+            out[b, s] = fn(np.ascontiguousarray(x[b, s]).reshape(-1), H, D, pos0 + s, theta).reshape(H, D)
+    return out
+
+
+@pytest.mark.parametrize("dtype,mode", [(oracle.BF16, "neox"), (oracle.F16, "neox"), (oracle.F32, "neox"),
+                                        (oracle.BF16, "gemma")])
+def test_prefill_rotated_keys_out_and_rope_modes(ctx, dtype, mode):
+    """k_rot_out receives the rotated keys in the input type (the reference's rotated cache rows), and the
+    Gemma rotation (double products) matches the oracle's applyRopeHalf restatement."""
+    import torch
+    import b200attn
+    B, S, Hq, Hkv, D, pos0, theta = 2, 70, 4, 2, 64, 5, 1e4
+    q = normal(31, (B, S, Hq, D), dtype)
+    k = normal(32, (B, S, Hkv, D), dtype)
+    v = normal(33, (B, S, Hkv, D), dtype)
+    scale = float(np.float32(1.0 / math.sqrt(D)))
+    q_rot = _rotate_rows(q, B=B, S=S, H=Hq, D=D, pos0=pos0, theta=theta, mode=mode)
+    k_rot = _rotate_rows(k, B=B, S=S, H=Hkv, D=D, pos0=pos0, theta=theta, mode=mode)
+    want = oracle.prefill(q_rot, k_rot, v, B=B, S=S, Hq=Hq, Hkv=Hkv, D=D, scale=scale, rope_theta=0.0)
+    tdt = getattr(torch, TORCH[dtype])
+    o = torch.empty((B, S, Hq, D), dtype=torch.float32, device="cuda")
+    kr = torch.empty((B, S, Hkv, D), dtype=tdt, device="cuda")
+    b200attn.prefill_causal(ctx, to_dev(q, dtype), to_dev(k, dtype), to_dev(v, dtype), o, scale,
+                            rope_mode=b200attn.ROPE_GEMMA if mode == "gemma" else b200attn.ROPE_NEOX,
+                            rope_theta=theta, pos0=pos0, k_rot_out=kr)
+    torch.cuda.synchronize()
+    assert_close(to_np(o), want, what=f"prefill {mode} {TORCH[dtype]}")
+    # rotated keys: the oracle rotation rounded to the input type, within one ulp of that type
+    got_k = to_np(kr)
+    want_k = oracle.round_to(k_rot, dtype)
+    ulp = {oracle.F16: 2.0 ** -10, oracle.BF16: 2.0 ** -7, oracle.F32: 2.0 ** -23}[dtype]
+    bound = ulp * np.maximum(np.abs(want_k), 2.0 ** -14)
+    assert np.all(np.abs(got_k - want_k) <= bound), float(np.max(np.abs(got_k - want_k) - bound))
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+def test_encoder_bf16_inputs(ctx, layout):
+    lens = [100, 37, 1, 64]
+    got, want = _encoder_case(ctx, B=4, H=3, S=100, D=64, dtype=oracle.BF16, lens=lens, layout=layout, seed=600)
+    assert_close(got, want, what="bf16 encoder")

@@ -364,9 +364,18 @@ B2A_API int b2a_mha(b2a_context* ctx, int in_dtype, int out_dtype, const void* q
         int rc = ensure_buffer(ctx, &ctx->pf_ws, &ctx->pf_ws_bytes, 3 * one, "encoder");
         if (rc) return rc;
         char* base = static_cast<char*>(ctx->pf_ws);
-        e = launch_convert(q, in_dtype, base, B2A_FLOAT16, (int64_t)n, ctx->status, s);
-        if (e == cudaSuccess) e = launch_convert(k, in_dtype, base + one, B2A_FLOAT16, (int64_t)n, ctx->status, s);
-        if (e == cudaSuccess) e = launch_convert(v, in_dtype, base + 2 * one, B2A_FLOAT16, (int64_t)n, ctx->status, s);
+        const void* ptrs[] = {q, k, v};
+        if (prep_vectorizable(D, ptrs, 3)) {  // one launch for the three conversions
+            const PrepJob jobs[3] = {PrepJob{q, base, nullptr, H, 0}, PrepJob{k, base + one, nullptr, H, 0},
+                                     PrepJob{v, base + 2 * one, nullptr, H, 0}};
+            e = launch_prep(jobs, 3, B, S, D, in_dtype, B2A_FLOAT16, 0, B2A_ROPE_NONE, nullptr, nullptr, ctx->status,
+                            s);
+        } else {
+            e = launch_convert(q, in_dtype, base, B2A_FLOAT16, (int64_t)n, ctx->status, s);
+            if (e == cudaSuccess) e = launch_convert(k, in_dtype, base + one, B2A_FLOAT16, (int64_t)n, ctx->status, s);
+            if (e == cudaSuccess)
+                e = launch_convert(v, in_dtype, base + 2 * one, B2A_FLOAT16, (int64_t)n, ctx->status, s);
+        }
         if (e != cudaSuccess) return cuda_fail(ctx, e, "conversion kernel launch");
         p.q = base;
         p.k = base + one;
@@ -446,7 +455,21 @@ B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype, co
     void* k_c = k_in_out ? k_rot_out : base + table_bytes + q_bytes;
     void* v_c = base + table_bytes + q_bytes + k_bytes;
     cudaError_t e = cudaSuccess;
-    if (rope) {
+    const void* prep_ptrs[] = {q, k, v, q_c, k_c, v_c, k_rot_out};
+    const bool vec_prep = (rope || conv) && prep_vectorizable(D, prep_ptrs, 7);
+    if (vec_prep) {
+        // one table build + one launch: q and k rotated / converted, v converted
+        double inv[kMaxHeadDim / 2] = {};
+        if (rope) inv_freq_table(rope_theta, D, inv);
+        PrepJob jobs[3];
+        int nj = 0;
+        jobs[nj++] = PrepJob{q, q_c, nullptr, Hq, rope ? 1 : 0};
+        jobs[nj++] = PrepJob{k, k_c, (rope && k_rot_out && !k_in_out) ? k_rot_out : nullptr, Hkv, rope ? 1 : 0};
+        if (conv) jobs[nj++] = PrepJob{v, v_c, nullptr, Hkv, 0};
+        e = launch_prep(jobs, nj, B, S, D, in_dtype, cdt, pos0, rope_mode, inv, table, ctx->status, s);
+        if (e == cudaSuccess && !rope && k_rot_out)
+            e = cudaMemcpyAsync(k_rot_out, k, nk * dtype_size(in_dtype), cudaMemcpyDeviceToDevice, s);
+    } else if (rope) {
         double inv[kMaxHeadDim / 2];
         inv_freq_table(rope_theta, D, inv);
         e = launch_rope_rows_with_table(q, in_dtype, q_c, cdt, B, S, Hq, D, p.q_sb, p.q_ss, p.q_sh, p.q_sb, p.q_ss,
@@ -465,7 +488,7 @@ B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype, co
         if (e == cudaSuccess && k_rot_out)
             e = cudaMemcpyAsync(k_rot_out, k, nk * dtype_size(in_dtype), cudaMemcpyDeviceToDevice, s);
     }
-    if (e == cudaSuccess && conv) e = launch_convert(v, in_dtype, v_c, cdt, (int64_t)nk, ctx->status, s);
+    if (e == cudaSuccess && conv && !vec_prep) e = launch_convert(v, in_dtype, v_c, cdt, (int64_t)nk, ctx->status, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "rope / conversion kernel launch");
     if (rope || conv) {
         p.q = q_c;

@@ -2,25 +2,30 @@
 // encoder) on the 5th-generation tensor cores: tcgen05.mma with TMEM
 // accumulators, TMA-staged Q/K/V tiles, mbarrier pipeline.
 //
-// CTA = two tiles of 128 query rows (A and B) of one (batch, head), 320 threads:
+// CTA = two tiles of 128 query rows (A and B) of one (batch, head), 384 threads
+// in three warpgroups:
 //   warps 0-3  softmax of tile A, warps 4-7 softmax of tile B: thread t of a
 //              group owns query row t = TMEM lane t (tcgen05.ld/st 32x32b);
 //   warp 8     TMA producer: Q_A, Q_B once, then K and V tiles of 128 keys
 //              into a 2-3 stage ring (plain tiled loads, 128-byte swizzle,
 //              64-element panels of the head dimension);
-//   warp 9     MMA issuer (one thread).  Per key tile j it issues
-//              O_A += P_A(j) V_j, S_A = Q_A K_{j+1}^T, O_B += P_B(j) V_j,
-//              S_B = Q_B K_{j+1}^T, so the tensor core works on one tile while
-//              the softmax group of the other runs (ping-pong).
+//   warp 9     MMA issuer (the whole warp runs the loop, lane 0 issues).  Per
+//              key tile j: O_A += P_A(j) V_j, S_A = Q_A K_{j+1}^T, then the same
+//              for B, so the tensor core works on one tile while the softmax
+//              group of the other runs (ping-pong);
+//   warps 10-11 idle.
+// setmaxnreg moves registers from the control warpgroup (8-11) to the softmax
+// warpgroups, which keep a whole score row (128 fp32) in registers.
 // TMEM (512 columns): S_A 0..127, S_B 128..255 (fp32 scores; the softmax
 // writes P as fp16 pairs over the first 64 columns, and the PV MMA reads it
 // from TMEM), O_A at 256, O_B at 384.
-// Softmax: two TMEM passes per tile (row max, then exp2 + row sum + P);
-// masks only on tiles that touch the causal diagonal, the window start or the
-// key end; the scale is folded into one FFMA per score; half of the exp2 run
-// on the FMA pipe as a degree-4 polynomial (see exp2_poly) to offload the
-// 16/clk/SM MUFU unit.  The running maximum moves lazily: O is rescaled only
-// when a row's maximum grows by more than 8 (log2 units), so P <= 2^8.
+// Softmax per tile: one TMEM read of the score row, row max (3-input max),
+// exp2 + row sum + P (f32x2 FMA/add); masks only on tiles that touch the
+// causal diagonal, the window start or the key end (a per-row visible key
+// range); the scale is folded into one FMA per score; a quarter of the exp2
+// run on the FMA pipe as a polynomial (exp2_poly_pair) next to the 16/clk/SM
+// MUFU.  The running maximum moves lazily: O is rescaled only when a row's
+// maximum grows by more than 8 (log2 units), so P <= 2^8.
 //
 // Every mbarrier wait is bounded by %globaltimer (kWaitNs).  On a timeout the
 // kernel sets status bit 3; other roles stop at their next wait; the producer
@@ -29,6 +34,7 @@
 //
 // Same semantics as attn_simt.cu / attn_mma.cu (the reference citations are
 // there); operands are fp16 (bf16 callers are converted by the host layer).
+// The additive [B][S] key mask has its own instantiation (kAdditive).
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -159,31 +165,7 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]
-__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-    uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3));
-}
-// D[tmem] (+)= A[tmem] * B[smem desc]
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-    uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3));
-}
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-                 : "memory");
-}
-// Warp-wide forms of the three: the whole warp computes the (warp-uniform)
+// MMA issue and commit, warp-wide: the whole warp computes the (warp-uniform)
 // operands and lane 0 alone issues, so the descriptors stay in the uniform
 // datapath instead of being moved there for every instruction.
 // Descriptors travel as two 32-bit words: only the low word (start address and
@@ -272,25 +254,13 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// 2^x without the XU pipe (which the MUFU exp2 and the fp16 packing already
-// load): x = n + f with n = round(x) taken by adding 1.5 * 2^23 (the FP adder
+// 2^x on the FMA pipe instead of the MUFU: x = n + f with n = round(x) taken by adding 1.5 * 2^23 (the FP adder
 // rounds to an integer; n is then in the low mantissa bits), f in
 // [-0.5, 0.5]; 2^f by a degree-4 polynomial fitted here to 2^f on
 // [-0.5, 0.5] (least squares on Chebyshev nodes with relative-error
 // reweighting; max relative error 8.5e-6, far below the fp16 rounding of P);
 // 2^n added to the exponent field.  x is clamped at -126 so the exponent
 // stays non-negative: masked scores (-inf) give 2^-126, which is 0 in fp16.
-__device__ __forceinline__ float exp2_poly(float x) {
-    x = fmaxf(x, -126.f);
-    const float t = x + 12582912.f;                     // 1.5 * 2^23
-    const int ni = __float_as_int(t) - 0x4B400000;      // round(x) as an integer
-    const float f = x - (t - 12582912.f);
-    float p = fmaf(0.009254964f, f, 0.05585603f);
-    p = fmaf(p, f, 0.24031252f);
-    p = fmaf(p, f, 0.6931306f);
-    p = fmaf(p, f, 0.9999978f);
-    return __int_as_float(__float_as_int(p) + (ni << 23));
-}
 
 // Pairs of fp32 in one 64-bit register: the f32x2 instructions of sm_100 do two
 // lanes per issue slot on the FMA pipe.
@@ -318,8 +288,7 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
 }
-// exp2_poly on a pair: the same operations, rounding and polynomial, two lanes
-// per f32x2 instruction.
+// Two of them per call, two lanes per f32x2 instruction.
 __device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& e0, float& e1) {
     const f32x2 x = f2_make(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
     const f32x2 t = f2_add(x, f2_make(12582912.f, 12582912.f));

@@ -93,6 +93,21 @@ cudaError_t launch_rope_rows_with_table(const void* src, int src_dtype, void* ds
                                         int pos0, int rope_mode, const double* inv_freq, double2* table,
                                         bool build_table, int* status, cudaStream_t stream);
 
+// Vectorised prefill pre-pass (D a multiple of 16, 16-byte aligned tensors):
+// each job rotates (rope_mode 1/2) or converts a dense [B][S][H][D] tensor into
+// out_dtype at dst, and, if dst_in is set, also writes the rotated rows in the
+// input dtype there.  One table build plus one launch for all jobs (at most 3).
+struct PrepJob {
+    const void* src;
+    void* dst;
+    void* dst_in;
+    int H;
+    int rotate;
+};
+bool prep_vectorizable(int D, const void* const* ptrs, int n);
+cudaError_t launch_prep(const PrepJob* jobs, int n_jobs, int B, int S, int D, int in_dtype, int out_dtype, int pos0,
+                        int rope_mode, const double* inv_freq, double2* table, int* status, cudaStream_t stream);
+
 // Sets the message b2a_last_error(NULL, ...) returns on this thread.
 void set_thread_error(const char* msg);
 

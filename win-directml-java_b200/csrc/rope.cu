@@ -74,6 +74,118 @@ __global__ void rope_rows_kernel(const void* src, int src_dtype, void* dst, int 
     }
 }
 
+// ---------------------------------------------------------------- vectorised pre-pass
+// One launch prepares all operands of a prefill: rows of q and k are rotated
+// (and converted), v is converted; every thread moves 8 elements of each half
+// of a row (16-byte accesses for 16-bit types).
+struct PrepSeg {
+    const void* src;
+    void* dst;       // compute dtype
+    void* dst_in;    // optional second copy in the input dtype (rotated keys for the caller)
+    int64_t units;   // rotated: rows * (D/2)/8; plain: elements / 8
+    int H;
+    int rotate;
+};
+struct PrepParams {
+    PrepSeg seg[3];
+    int n_seg;
+    int S, D, half, chunks;
+    int in_dtype, out_dtype, rope_mode;
+    const double2* table;
+    int* status;
+};
+
+__device__ __forceinline__ void load8(const void* base, int64_t e, int dtype, float* x) {
+    if (dtype == kF32) {
+        const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + e);
+        const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + e + 4);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+        return;
+    }
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + e);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (dtype == kBF16) {
+            x[2 * i] = __uint_as_float(w[i] << 16);
+            x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        } else {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            x[2 * i] = f.x;
+            x[2 * i + 1] = f.y;
+        }
+    }
+}
+__device__ __forceinline__ void store8(void* base, int64_t e, int dtype, const float* x, int* status) {
+    if (dtype == kF32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(base) + e) = make_float4(x[0], x[1], x[2], x[3]);
+        *reinterpret_cast<float4*>(static_cast<float*>(base) + e + 4) = make_float4(x[4], x[5], x[6], x[7]);
+        return;
+    }
+    uint32_t w[4];
+    bool over = false;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (dtype == kBF16) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&h);
+            const float2 r = __bfloat1622float2(h);
+            over |= (isinf(r.x) && !isinf(x[2 * i])) || (isinf(r.y) && !isinf(x[2 * i + 1]));
+        } else {
+            const __half2 h = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&h);
+            const float2 r = __half22float2(h);
+            over |= (isinf(r.x) && !isinf(x[2 * i])) || (isinf(r.y) && !isinf(x[2 * i + 1]));
+        }
+    }
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + e) = make_uint4(w[0], w[1], w[2], w[3]);
+    if (over && status != nullptr) atomicOr(status, 4);
+}
+
+__global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ PrepParams p) {
+    // the segments one after another, each over the whole grid
+#pragma unroll
+    for (int sgi = 0; sgi < 3; ++sgi) {
+        if (sgi >= p.n_seg) break;
+        const PrepSeg& sg = p.seg[sgi];
+        for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < sg.units;
+             u += (int64_t)gridDim.x * blockDim.x) {
+            if (!sg.rotate) {
+                float x[8];
+                load8(sg.src, u * 8, p.in_dtype, x);
+                store8(sg.dst, u * 8, p.out_dtype, x, p.status);
+                continue;
+            }
+            const int64_t row = u / p.chunks;
+            const int i0 = (int)(u - row * p.chunks) * 8;
+            const int s = (int)((row / sg.H) % p.S);
+            const int64_t e0 = row * p.D + i0, e1 = e0 + p.half;
+            float a[8], c[8], y0[8], y1[8];
+            load8(sg.src, e0, p.in_dtype, a);
+            load8(sg.src, e1, p.in_dtype, c);
+            const double2* cs = p.table + (int64_t)s * p.half + i0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const double2 t = cs[i];
+                if (p.rope_mode == 2) {
+                    y0[i] = (float)__dsub_rn(__dmul_rn((double)a[i], t.x), __dmul_rn((double)c[i], t.y));
+                    y1[i] = (float)__dadd_rn(__dmul_rn((double)c[i], t.x), __dmul_rn((double)a[i], t.y));
+                } else {
+                    const float cf = (float)t.x, sf = (float)t.y;
+                    y0[i] = __fsub_rn(__fmul_rn(a[i], cf), __fmul_rn(c[i], sf));
+                    y1[i] = __fadd_rn(__fmul_rn(a[i], sf), __fmul_rn(c[i], cf));
+                }
+            }
+            store8(sg.dst, e0, p.out_dtype, y0, p.status);
+            store8(sg.dst, e1, p.out_dtype, y1, p.status);
+            if (sg.dst_in != nullptr) {
+                store8(sg.dst_in, e0, p.in_dtype, y0, nullptr);
+                store8(sg.dst_in, e1, p.in_dtype, y1, nullptr);
+            }
+        }
+    }
+}
+
 }  // namespace
 
 // `table` is a device buffer of S * D/2 double2 entries owned by the caller;
@@ -106,6 +218,55 @@ cudaError_t launch_convert(const void* src, int src_dtype, void* dst, int dst_dt
     const int64_t blocks = (n + 255) / 256;
     const int grid = (int)(blocks < 148 * 32 ? blocks : 148 * 32);
     convert_kernel<<<grid, 256, 0, stream>>>(src, src_dtype, dst, dst_dtype, n, status);
+    return cudaGetLastError();
+}
+
+bool prep_vectorizable(int D, const void* const* ptrs, int n) {
+    if (D % 16 != 0) return false;  // D/2 a multiple of 8
+    for (int i = 0; i < n; ++i)
+        if (ptrs[i] != nullptr && reinterpret_cast<uintptr_t>(ptrs[i]) % 16 != 0) return false;
+    return true;
+}
+
+cudaError_t launch_prep(const PrepJob* jobs, int n_jobs, int B, int S, int D, int in_dtype, int out_dtype, int pos0,
+                        int rope_mode, const double* inv_freq, double2* table, int* status, cudaStream_t stream) {
+    const int half = D / 2;
+    bool any_rotate = false;
+    for (int i = 0; i < n_jobs; ++i) any_rotate |= jobs[i].rotate != 0;
+    if (any_rotate) {
+        FreqTable f{};
+        for (int i = 0; i < half; ++i) f.inv_freq[i] = inv_freq[i];
+        const int64_t n = (int64_t)S * half;
+        const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+        rope_table_kernel<<<grid, 256, 0, stream>>>(table, S, half, pos0, f);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    PrepParams p{};
+    p.S = S;
+    p.D = D;
+    p.half = half;
+    p.chunks = half / 8;
+    p.in_dtype = in_dtype;
+    p.out_dtype = out_dtype;
+    p.rope_mode = rope_mode;
+    p.table = table;
+    p.status = status;
+    int64_t most = 0;
+    for (int i = 0; i < n_jobs && i < 3; ++i) {
+        PrepSeg& sg = p.seg[p.n_seg++];
+        sg.src = jobs[i].src;
+        sg.dst = jobs[i].dst;
+        sg.dst_in = jobs[i].dst_in;
+        sg.H = jobs[i].H;
+        sg.rotate = jobs[i].rotate;
+        const int64_t elems = (int64_t)B * S * jobs[i].H * D;
+        sg.units = sg.rotate ? elems / 16 : elems / 8;  // rotated units move 8 + 8 elements
+        most = sg.units > most ? sg.units : most;
+    }
+    const int64_t blocks = (most + 255) / 256;
+    const int grid = (int)(blocks < 148 * 16 ? blocks : 148 * 16);
+    prep_kernel<<<grid, 256, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
