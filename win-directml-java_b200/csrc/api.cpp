@@ -365,7 +365,7 @@ B2A_API int b2a_mha(b2a_context* ctx, int in_dtype, int out_dtype, const void* q
         if (rc) return rc;
         char* base = static_cast<char*>(ctx->pf_ws);
         const void* ptrs[] = {q, k, v};
-        if (prep_vectorizable(D, ptrs, 3)) {  // one launch for the three conversions
+        if (prep_vectorizable(D, (int64_t)n, ptrs, 3)) {  // one launch for the three conversions
             const PrepJob jobs[3] = {PrepJob{q, base, nullptr, H, 0}, PrepJob{k, base + one, nullptr, H, 0},
                                      PrepJob{v, base + 2 * one, nullptr, H, 0}};
             e = launch_prep(jobs, 3, B, S, D, in_dtype, B2A_FLOAT16, 0, B2A_ROPE_NONE, nullptr, nullptr, ctx->status,
@@ -456,7 +456,7 @@ B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype, co
     void* v_c = base + table_bytes + q_bytes + k_bytes;
     cudaError_t e = cudaSuccess;
     const void* prep_ptrs[] = {q, k, v, q_c, k_c, v_c, k_rot_out};
-    const bool vec_prep = (rope || conv) && prep_vectorizable(D, prep_ptrs, 7);
+    const bool vec_prep = (rope || conv) && prep_vectorizable(D, (int64_t)std::max(nq, nk), prep_ptrs, 7);
     if (vec_prep) {
         // one table build + one launch: q and k rotated / converted, v converted
         double inv[kMaxHeadDim / 2] = {};

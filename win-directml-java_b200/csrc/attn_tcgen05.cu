@@ -93,7 +93,7 @@ struct TcGeo {
     static constexpr int oV = oK + kStages * kTileBytes;
     static constexpr int oBar = oV + kStages * kTileBytes;
     static constexpr int kBytes = oBar + 512;
-    static constexpr uint32_t kTxKV = 2 * kTileBytes;
+    static constexpr uint32_t kTxTile = kTileBytes;  // bytes one K or V tile load delivers (zero fill included)
     static_assert(kBytes + 1024 <= 227 * 1024, "shared memory budget");
 };
 
@@ -346,12 +346,16 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const uint32_t bar0 = base + Gm::oBar;
     // barriers, 8 bytes each
     const uint32_t bQ = bar0;
-    auto bKVfull = [&](int s) { return bar0 + 8u * (1 + s); };
-    auto bKVempty = [&](int s) { return bar0 + 8u * (1 + ST + s); };
-    auto bSfull = [&](int t) { return bar0 + 8u * (1 + 2 * ST + t); };
-    auto bPfull = [&](int t) { return bar0 + 8u * (3 + 2 * ST + t); };
-    auto bOdone = [&](int t) { return bar0 + 8u * (5 + 2 * ST + t); };
-    const uint32_t bDrain = bar0 + 8u * (7 + 2 * ST);
+    // K and V have separate rings: K(j) is last read by QK(j) one step before V(j) is
+    // last read by PV(j), so its stage is refilled that much earlier
+    auto bKfull = [&](int s) { return bar0 + 8u * (1 + s); };
+    auto bKempty = [&](int s) { return bar0 + 8u * (1 + ST + s); };
+    auto bVfull = [&](int s) { return bar0 + 8u * (1 + 2 * ST + s); };
+    auto bVempty = [&](int s) { return bar0 + 8u * (1 + 3 * ST + s); };
+    auto bSfull = [&](int t) { return bar0 + 8u * (1 + 4 * ST + t); };
+    auto bPfull = [&](int t) { return bar0 + 8u * (3 + 4 * ST + t); };
+    auto bOdone = [&](int t) { return bar0 + 8u * (5 + 4 * ST + t); };
+    const uint32_t bDrain = bar0 + 8u * (7 + 4 * ST);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(base_ptr + Gm::oBar + 256);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(base_ptr + Gm::oBar + 264);
 
@@ -392,8 +396,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     if (tid == 0) {
         mbar_init(bQ, 1);
         for (int s = 0; s < ST; ++s) {
-            mbar_init(bKVfull(s), 1);
-            mbar_init(bKVempty(s), 1);
+            mbar_init(bKfull(s), 1);
+            mbar_init(bKempty(s), 1);
+            mbar_init(bVfull(s), 1);
+            mbar_init(bVempty(s), 1);
         }
         for (int t = 0; t < 2; ++t) {
             mbar_init(bSfull(t), 1);
@@ -420,27 +426,36 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       if (warp == 8) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            int issued = 0;
+            int k_issued = 0, v_issued = 0;
+            // one K or V tile into its ring stage, after the stage's previous tile was released
+            auto load = [&](const CUtensorMap* map, uint32_t ring, int j, bool is_k) -> bool {
+                const int st = j % ST;
+                const uint32_t full = is_k ? bKfull(st) : bVfull(st), empty = is_k ? bKempty(st) : bVempty(st);
+                if (j >= ST && !mbar_wait(empty, ((j / ST) - 1) & 1, abort_flag, status)) return false;
+                mbar_expect_tx(full, Gm::kTxTile);
+                for (int pn = 0; pn < NP; ++pn)
+                    tma_load_4d(ring + st * Gm::kTileBytes + pn * Gm::kPanelBytes, map, full, 64 * pn, kvh,
+                                (t_begin + j) * kBN, b);
+                return true;
+            };
             mbar_expect_tx(bQ, 2 * Gm::kTileBytes);
             for (int t = 0; t < 2; ++t)
                 for (int pn = 0; pn < NP; ++pn)
                     tma_load_4d(sQ + t * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmQ, bQ, 64 * pn, h, q0t[t], b);
-            for (int j = 0; j < n_max; ++j) {
-                const int st = j % ST;
-                if (j >= ST && !mbar_wait(bKVempty(st), ((j / ST) - 1) & 1, abort_flag, status)) break;
-                const int n0 = (t_begin + j) * kBN;
-                mbar_expect_tx(bKVfull(st), Gm::kTxKV);
-                for (int pn = 0; pn < NP; ++pn) {
-                    tma_load_4d(sK + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmK, bKVfull(st), 64 * pn, kvh, n0,
-                                b);
-                    tma_load_4d(sV + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmV, bKVfull(st), 64 * pn, kvh, n0,
-                                b);
+            // K runs one tile ahead of V: K(0), then K(i+1), V(i)
+            if (n_max > 0 && load(&tmK, sK, 0, true)) k_issued = 1;
+            for (int i = 0; i < n_max && k_issued > i; ++i) {
+                if (i + 1 < n_max) {
+                    if (!load(&tmK, sK, i + 1, true)) break;
+                    k_issued = i + 2;
                 }
-                issued = j + 1;
+                if (!load(&tmV, sV, i, false)) break;
+                v_issued = i + 1;
             }
             // every copy this thread issued lands before the CTA may exit
             mbar_drain(bQ, 0);
-            for (int j = (issued > ST ? issued - ST : 0); j < issued; ++j) mbar_drain(bKVfull(j % ST), (j / ST) & 1);
+            for (int j = (k_issued > ST ? k_issued - ST : 0); j < k_issued; ++j) mbar_drain(bKfull(j % ST), (j / ST) & 1);
+            for (int j = (v_issued > ST ? v_issued - ST : 0); j < v_issued; ++j) mbar_drain(bVfull(j % ST), (j / ST) & 1);
         }
     } else if (warp == 9) {
         // ------------------------------------------------------------ MMA issuer
@@ -450,16 +465,26 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             const uint32_t ln = (uint32_t)lane;
             const uint32_t idq = make_idesc(p.fmt, kBM, kBN, 0, 0);
             const uint32_t idp = make_idesc(p.fmt, kBM, D, 0, 1);
-            int kv_ready = -1;  // highest key tile whose K/V wait was observed
+            int k_ready = -1, v_ready = -1;  // highest key tile whose K / V wait was observed
             bool ok = __all_sync(0xffffffffu, mbar_wait(bQ, 0, abort_flag, status));
-            auto wait_kv = [&](int j) -> bool {
-                if (kv_ready >= j) return true;
-                if (!__all_sync(0xffffffffu, mbar_wait(bKVfull(j % ST), (j / ST) & 1, abort_flag, status)))
+            auto wait_k = [&](int j) -> bool {
+                if (k_ready >= j) return true;
+                if (!__all_sync(0xffffffffu, mbar_wait(bKfull(j % ST), (j / ST) & 1, abort_flag, status)))
                     return false;
                 tc_fence_after();
-                kv_ready = j;
+                k_ready = j;
                 return true;
             };
+            auto wait_v = [&](int j) -> bool {
+                if (v_ready >= j) return true;
+                if (!__all_sync(0xffffffffu, mbar_wait(bVfull(j % ST), (j / ST) & 1, abort_flag, status)))
+                    return false;
+                tc_fence_after();
+                v_ready = j;
+                return true;
+            };
+            // the tile that reads K(j) / V(j) last (tile B unless it has no key tile j)
+            auto last_tile = [&](int j) { return j < nt[1] ? 1 : 0; };
             // descriptors of each buffer's start: a K step, tile or stage offset only moves the
             // 14-bit start-address field (addr >> 4) of the low word, and every offset here stays inside it
             const uint64_t dQ = smem_desc(sQ, 16, 1024), dK = smem_desc(sK, 16, 1024);
@@ -488,9 +513,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 umma_commit_w(ln, bOdone(t));
             };
             if (ok && n_max > 0) {
-                ok = wait_kv(0);
+                ok = wait_k(0);
                 for (int t = 0; t < 2 && ok; ++t)
                     if (nt[t] > 0) issue_qk(t, 0);
+                if (ok) umma_commit_w(ln, bKempty(0));
             }
             for (int j = 0; j < n_max && ok; ++j) {
                 // rolled over the two tiles: unrolled, each tile's per-step descriptor words
@@ -503,16 +529,21 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                         break;
                     }
                     tc_fence_after();
+                    if (!wait_v(j)) {
+                        ok = false;
+                        break;
+                    }
                     issue_pv(t, j);
+                    if (t == last_tile(j)) umma_commit_w(ln, bVempty(j % ST));  // V(j) read for the last time
                     if (j + 1 < nt[t]) {
-                        if (!wait_kv(j + 1)) {
+                        if (!wait_k(j + 1)) {
                             ok = false;
                             break;
                         }
                         issue_qk(t, j + 1);
+                        if (t == last_tile(j + 1)) umma_commit_w(ln, bKempty((j + 1) % ST));
                     }
                 }
-                umma_commit_w(ln, bKVempty(j % ST));  // stage j is free once both PV(j) finish
             }
             // all MMAs lane 0 issued are complete before TMEM is released
             umma_commit_w(ln, bDrain);

@@ -104,7 +104,8 @@ struct PrepJob {
     int H;
     int rotate;
 };
-bool prep_vectorizable(int D, const void* const* ptrs, int n);
+// elems: the largest tensor's element count.
+bool prep_vectorizable(int D, int64_t elems, const void* const* ptrs, int n);
 cudaError_t launch_prep(const PrepJob* jobs, int n_jobs, int B, int S, int D, int in_dtype, int out_dtype, int pos0,
                         int rope_mode, const double* inv_freq, double2* table, int* status, cudaStream_t stream);
 

@@ -28,6 +28,18 @@ __global__ void rope_table_kernel(double2* table, int S, int half, int pos0, con
     }
 }
 
+// Same angles, stored as the float (cos, sin) the NeoX rotation multiplies with
+// (the double values rounded to float): half the bytes of the double table.
+__global__ void rope_table_f32_kernel(float2* table, int S, int half, int pos0, const __grid_constant__ FreqTable f) {
+    const int64_t n = (int64_t)S * half;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int s = (int)(e / half), i = (int)(e - (int64_t)s * half);
+        double sn, cn;
+        sincos((double)(pos0 + s) * f.inv_freq[i], &sn, &cn);
+        table[e] = make_float2((float)cn, (float)sn);
+    }
+}
+
 // Flags (status bit 2) a finite input that became infinite in the
 // destination type: bf16 operands above the fp16 range.
 __device__ __forceinline__ void flag_overflow(float in, float out, int* status) {
@@ -82,7 +94,7 @@ struct PrepSeg {
     const void* src;
     void* dst;       // compute dtype
     void* dst_in;    // optional second copy in the input dtype (rotated keys for the caller)
-    int64_t units;   // rotated: rows * (D/2)/8; plain: elements / 8
+    int64_t units;   // rotated: B * S * head groups * (D/2)/8; plain: elements / 8
     int H;
     int rotate;
 };
@@ -91,31 +103,10 @@ struct PrepParams {
     int n_seg;
     int S, D, half, chunks;
     int in_dtype, out_dtype, rope_mode;
-    const double2* table;
+    const void* table;  // float2 (NeoX) or double2 (Gemma) (cos, sin) per (position, pair)
     int* status;
 };
 
-__device__ __forceinline__ void load8(const void* base, int64_t e, int dtype, float* x) {
-    if (dtype == kF32) {
-        const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + e);
-        const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + e + 4);
-        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-        return;
-    }
-    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + e);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        if (dtype == kBF16) {
-            x[2 * i] = __uint_as_float(w[i] << 16);
-            x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-        } else {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-            x[2 * i] = f.x;
-            x[2 * i + 1] = f.y;
-        }
-    }
-}
 __device__ __forceinline__ void store8(void* base, int64_t e, int dtype, const float* x, int* status) {
     if (dtype == kF32) {
         *reinterpret_cast<float4*>(static_cast<float*>(base) + e) = make_float4(x[0], x[1], x[2], x[3]);
@@ -142,45 +133,145 @@ __device__ __forceinline__ void store8(void* base, int64_t e, int dtype, const f
     if (over && status != nullptr) atomicOr(status, 4);
 }
 
-__global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ PrepParams p) {
+// 8 raw elements (16 bytes of a 16-bit type, 32 of fp32), loaded before any
+// arithmetic so that each thread has all its loads in flight at once.
+template <bool kF32In>
+struct Raw8 {
+    uint4 w[kF32In ? 2 : 1];
+};
+template <bool kF32In>
+__device__ __forceinline__ Raw8<kF32In> raw_load(const void* base, int64_t e) {
+    Raw8<kF32In> r;
+    if (kF32In) {
+        r.w[0] = *reinterpret_cast<const uint4*>(static_cast<const float*>(base) + e);
+        r.w[kF32In ? 1 : 0] = *reinterpret_cast<const uint4*>(static_cast<const float*>(base) + e + 4);
+    } else {
+        r.w[0] = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + e);
+    }
+    return r;
+}
+template <bool kF32In>
+__device__ __forceinline__ void raw_unpack(const Raw8<kF32In>& r, int dtype, float* x) {
+    if (kF32In) {
+        const uint4 a = r.w[0], b = r.w[kF32In ? 1 : 0];
+        x[0] = __uint_as_float(a.x); x[1] = __uint_as_float(a.y); x[2] = __uint_as_float(a.z); x[3] = __uint_as_float(a.w);
+        x[4] = __uint_as_float(b.x); x[5] = __uint_as_float(b.y); x[6] = __uint_as_float(b.z); x[7] = __uint_as_float(b.w);
+        return;
+    }
+    const uint32_t w[4] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (dtype == kBF16) {
+            x[2 * i] = __uint_as_float(w[i] << 16);
+            x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        } else {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            x[2 * i] = f.x;
+            x[2 * i + 1] = f.y;
+        }
+    }
+}
+
+// kMode 1: NeoX rotation in float; 2: Gemma rotation with double products.
+// kF32In: fp32 inputs (else 16-bit).  kHeads head rows per rotated unit; plain
+// conversion moves 2 * kHeads chunks per thread and pass.
+template <int kMode, bool kF32In, int kHeads>
+__global__ void __launch_bounds__(256, 2) prep_kernel(const __grid_constant__ PrepParams p) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     // the segments one after another, each over the whole grid
+#pragma unroll 1
+    for (int sgi = 0; sgi < p.n_seg; ++sgi) {
+        const PrepSeg sg = p.seg[sgi];
+        if (!sg.rotate) {
+            // plain conversion: 2 * kHeads chunks of 8 per thread and pass, stride apart (coalesced)
+            constexpr int kPlain = 2 * kHeads;
+            for (int64_t u = first; u < sg.units; u += kPlain * stride) {
+                Raw8<kF32In> r[kPlain];
 #pragma unroll
-    for (int sgi = 0; sgi < 3; ++sgi) {
-        if (sgi >= p.n_seg) break;
-        const PrepSeg& sg = p.seg[sgi];
-        for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < sg.units;
-             u += (int64_t)gridDim.x * blockDim.x) {
-            if (!sg.rotate) {
-                float x[8];
-                load8(sg.src, u * 8, p.in_dtype, x);
-                store8(sg.dst, u * 8, p.out_dtype, x, p.status);
-                continue;
-            }
-            const int64_t row = u / p.chunks;
-            const int i0 = (int)(u - row * p.chunks) * 8;
-            const int s = (int)((row / sg.H) % p.S);
-            const int64_t e0 = row * p.D + i0, e1 = e0 + p.half;
-            float a[8], c[8], y0[8], y1[8];
-            load8(sg.src, e0, p.in_dtype, a);
-            load8(sg.src, e1, p.in_dtype, c);
-            const double2* cs = p.table + (int64_t)s * p.half + i0;
+                for (int k = 0; k < kPlain; ++k)
+                    if (u + k * stride < sg.units) r[k] = raw_load<kF32In>(sg.src, (u + k * stride) * 8);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const double2 t = cs[i];
-                if (p.rope_mode == 2) {
-                    y0[i] = (float)__dsub_rn(__dmul_rn((double)a[i], t.x), __dmul_rn((double)c[i], t.y));
-                    y1[i] = (float)__dadd_rn(__dmul_rn((double)c[i], t.x), __dmul_rn((double)a[i], t.y));
-                } else {
-                    const float cf = (float)t.x, sf = (float)t.y;
-                    y0[i] = __fsub_rn(__fmul_rn(a[i], cf), __fmul_rn(c[i], sf));
-                    y1[i] = __fadd_rn(__fmul_rn(a[i], sf), __fmul_rn(c[i], cf));
+                for (int k = 0; k < kPlain; ++k) {
+                    if (u + k * stride >= sg.units) break;
+                    float x[8];
+                    raw_unpack<kF32In>(r[k], p.in_dtype, x);
+                    store8(sg.dst, (u + k * stride) * 8, p.out_dtype, x, p.status);
                 }
             }
-            store8(sg.dst, e0, p.out_dtype, y0, p.status);
-            store8(sg.dst, e1, p.out_dtype, y1, p.status);
-            if (sg.dst_in != nullptr) {
-                store8(sg.dst_in, e0, p.in_dtype, y0, nullptr);
-                store8(sg.dst_in, e1, p.in_dtype, y1, nullptr);
+            continue;
+        }
+        // rotated: unit = (b, s, head group, chunk); the chunk's 8 (cos, sin) pairs are read
+        // once and applied to the kHeads rows of the group
+        // 32-bit index arithmetic (the host keeps units below 2^31): 64-bit division is a
+        // long emulated sequence and dominated this loop
+        const uint32_t groups = (uint32_t)(sg.H + kHeads - 1) / kHeads, chunks = (uint32_t)p.chunks;
+        for (int64_t u = first; u < sg.units; u += stride) {
+            const uint32_t uu = (uint32_t)u;
+            const uint32_t rest = uu / chunks;
+            const int chunk = (int)(uu - rest * chunks);
+            const uint32_t bs32 = rest / groups;
+            const int g = (int)(rest - bs32 * groups);
+            const int64_t bs = bs32;
+            const int i0 = chunk * 8;
+            const int s = (int)(bs32 % (uint32_t)p.S);
+            Raw8<kF32In> ra[kHeads], rc[kHeads];
+#pragma unroll
+            for (int k = 0; k < kHeads; ++k) {
+                const int h = g * kHeads + k;
+                if (h < sg.H) {
+                    const int64_t e0 = (bs * sg.H + h) * p.D + i0;
+                    ra[k] = raw_load<kF32In>(sg.src, e0);
+                    rc[k] = raw_load<kF32In>(sg.src, e0 + p.half);
+                }
+            }
+            // the chunk's 8 (cos, sin) pairs, once per unit, into registers
+            float cf[8], sf[8];
+            double cd[8], sd[8];
+            if (kMode == 2) {
+                const double2* cs = static_cast<const double2*>(p.table) + (int64_t)s * p.half + i0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const double2 t = cs[i];
+                    cd[i] = t.x;
+                    sd[i] = t.y;
+                }
+            } else {
+                const float4* cs = reinterpret_cast<const float4*>(static_cast<const float2*>(p.table) +
+                                                                   (int64_t)s * p.half + i0);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float4 t = cs[i];
+                    cf[2 * i] = t.x;
+                    sf[2 * i] = t.y;
+                    cf[2 * i + 1] = t.z;
+                    sf[2 * i + 1] = t.w;
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < kHeads; ++k) {
+                const int h = g * kHeads + k;
+                if (h >= sg.H) break;
+                const int64_t e0 = (bs * sg.H + h) * p.D + i0, e1 = e0 + p.half;
+                float a[8], c[8], y0[8], y1[8];
+                raw_unpack<kF32In>(ra[k], p.in_dtype, a);
+                raw_unpack<kF32In>(rc[k], p.in_dtype, c);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    if (kMode == 2) {
+                        y0[i] = (float)__dsub_rn(__dmul_rn((double)a[i], cd[i]), __dmul_rn((double)c[i], sd[i]));
+                        y1[i] = (float)__dadd_rn(__dmul_rn((double)c[i], cd[i]), __dmul_rn((double)a[i], sd[i]));
+                    } else {
+                        y0[i] = __fsub_rn(__fmul_rn(a[i], cf[i]), __fmul_rn(c[i], sf[i]));
+                        y1[i] = __fadd_rn(__fmul_rn(a[i], sf[i]), __fmul_rn(c[i], cf[i]));
+                    }
+                }
+                store8(sg.dst, e0, p.out_dtype, y0, p.status);
+                store8(sg.dst, e1, p.out_dtype, y1, p.status);
+                if (sg.dst_in != nullptr) {
+                    store8(sg.dst_in, e0, p.in_dtype, y0, nullptr);
+                    store8(sg.dst_in, e1, p.in_dtype, y1, nullptr);
+                }
             }
         }
     }
@@ -221,8 +312,9 @@ cudaError_t launch_convert(const void* src, int src_dtype, void* dst, int dst_dt
     return cudaGetLastError();
 }
 
-bool prep_vectorizable(int D, const void* const* ptrs, int n) {
+bool prep_vectorizable(int D, int64_t elems, const void* const* ptrs, int n) {
     if (D % 16 != 0) return false;  // D/2 a multiple of 8
+    if (elems / 16 >= (int64_t)1 << 31) return false;  // rotated units are counted in 32 bits
     for (int i = 0; i < n; ++i)
         if (ptrs[i] != nullptr && reinterpret_cast<uintptr_t>(ptrs[i]) % 16 != 0) return false;
     return true;
@@ -238,7 +330,8 @@ cudaError_t launch_prep(const PrepJob* jobs, int n_jobs, int B, int S, int D, in
         for (int i = 0; i < half; ++i) f.inv_freq[i] = inv_freq[i];
         const int64_t n = (int64_t)S * half;
         const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
-        rope_table_kernel<<<grid, 256, 0, stream>>>(table, S, half, pos0, f);
+        if (rope_mode == 2) rope_table_kernel<<<grid, 256, 0, stream>>>(table, S, half, pos0, f);
+        else rope_table_f32_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<float2*>(table), S, half, pos0, f);
         const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
@@ -252,6 +345,9 @@ cudaError_t launch_prep(const PrepJob* jobs, int n_jobs, int B, int S, int D, in
     p.rope_mode = rope_mode;
     p.table = table;
     p.status = status;
+    // rotated rows per unit: fewer where the unit holds more registers (fp32 data, double cos/sin)
+    const bool gemma = rope_mode == 2;
+    const int heads = (in_dtype == kF32 ? 2 : 4) / (gemma ? 2 : 1);
     int64_t most = 0;
     for (int i = 0; i < n_jobs && i < 3; ++i) {
         PrepSeg& sg = p.seg[p.n_seg++];
@@ -260,13 +356,21 @@ cudaError_t launch_prep(const PrepJob* jobs, int n_jobs, int B, int S, int D, in
         sg.dst_in = jobs[i].dst_in;
         sg.H = jobs[i].H;
         sg.rotate = jobs[i].rotate;
-        const int64_t elems = (int64_t)B * S * jobs[i].H * D;
-        sg.units = sg.rotate ? elems / 16 : elems / 8;  // rotated units move 8 + 8 elements
-        most = sg.units > most ? sg.units : most;
+        const int64_t rows = (int64_t)B * S * jobs[i].H;
+        sg.units = sg.rotate ? (int64_t)B * S * ((jobs[i].H + heads - 1) / heads) * p.chunks : rows * D / 8;
+        const int64_t threads = sg.rotate ? sg.units : (sg.units + 2 * heads - 1) / (2 * heads);
+        most = threads > most ? threads : most;
     }
+    // 2 blocks of 256 per SM stay resident (about 128 registers a thread); a few passes of the largest segment
     const int64_t blocks = (most + 255) / 256;
-    const int grid = (int)(blocks < 148 * 16 ? blocks : 148 * 16);
-    prep_kernel<<<grid, 256, 0, stream>>>(p);
+    const int grid = (int)(blocks < 148 * 2 * 8 ? blocks : 148 * 2 * 8);
+    if (in_dtype != kF32) {
+        if (gemma) prep_kernel<2, false, 2><<<grid, 256, 0, stream>>>(p);
+        else prep_kernel<1, false, 4><<<grid, 256, 0, stream>>>(p);
+    } else {
+        if (gemma) prep_kernel<2, true, 1><<<grid, 256, 0, stream>>>(p);
+        else prep_kernel<1, true, 2><<<grid, 256, 0, stream>>>(p);
+    }
     return cudaGetLastError();
 }
 
