@@ -277,7 +277,7 @@ class DecodeWorkload:
 class PrefillWorkload:
     """c1 / c4: causal prefill with fused RoPE; c2: masked encoder."""
 
-    def __init__(self, name: str, seed: int):
+    def __init__(self, name: str, seed: int, batch: int = 0):
         import torch
         import b200attn
         import oracle
@@ -289,8 +289,10 @@ class PrefillWorkload:
             self.B, self.S, self.Hq, self.Hkv, self.D, self.dt, self.theta = 8, 4096, 32, 32, 96, torch.bfloat16, 1e4
         else:
             self.B, self.S, self.Hq, self.Hkv, self.D, self.dt, self.theta = 64, 128, 12, 12, 32, torch.float16, 0
-            self.lens = oracle.splitmix_uniform_int(seed, self.B, 16, 128)
+            self.lens = oracle.splitmix_uniform_int(seed, self.B if batch <= 0 else batch, 16, 128)
             self.lens_d = torch.from_numpy(self.lens).cuda()
+        if batch > 0:  # smaller batch for profiler captures only
+            self.B = batch
         mk = lambda h: torch.randn(self.B, self.S, h, self.D, generator=g, device="cuda").to(self.dt)
         self.q, self.k, self.v = mk(self.Hq), mk(self.Hkv), mk(self.Hkv)
         self.o = torch.empty_like(self.q)
@@ -300,7 +302,7 @@ class PrefillWorkload:
         return self.B * self.S
 
     def kernel_launches_per_step(self):
-        return 1 if self.name == "c2" else 4  # rope table, rope q, rope k, attention
+        return 1 if self.name == "c2" else 3  # rope table, one pre-pass (rope q, k; convert), attention
 
     def flops(self):
         if self.name == "c2":
@@ -450,7 +452,7 @@ def main():
     ap.add_argument("--workload", default="c5", choices=sorted(WORKLOADS))
     ap.add_argument("--no-suite", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--batch", type=int, default=0, help="override the decode batch (profiling captures only)")
+    ap.add_argument("--batch", type=int, default=0, help="override the batch (profiling captures only)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -476,7 +478,7 @@ def main():
     hbm, tflops, src = peaks()
 
     w = DecodeWorkload(args.workload, 5 + rank, args.batch) if args.workload in ("c3", "c5") else \
-        PrefillWorkload(args.workload, {"c1": 1, "c2": 2, "c4": 4}[args.workload])
+        PrefillWorkload(args.workload, {"c1": 1, "c2": 2, "c4": 4}[args.workload], args.batch)
     for _ in range(args.warmup):
         w.step(ctx)
     torch.cuda.synchronize()
