@@ -171,7 +171,7 @@ class ClockSampler:
 class DecodeWorkload:
     """configs[4] (c5) or configs[2] (c3): one decode token for every sequence."""
 
-    def __init__(self, name: str, seed: int, batch: int = 0):
+    def __init__(self, name: str, seed: int, batch: int = 0, world: int = 1, rank: int = 0):
         import torch
         import b200attn
         self.torch, self.b2a = torch, b200attn
@@ -186,9 +186,16 @@ class DecodeWorkload:
         if batch > 0:  # smaller batch for profiler captures only
             self.B = batch
         import oracle
-        self.lens = oracle.splitmix_uniform_int(seed, self.B, self.lo, self.hi)
+        # one global batch of world * B sequences; each rank takes its cost-balanced,
+        # equal-count shard (b200attn.sharding.plan_shards; cost = keys attended)
+        lens_all = oracle.splitmix_uniform_int(seed, self.B * world, self.lo, self.hi)
+        if world > 1:
+            from b200attn import sharding
+            self.lens = np.ascontiguousarray(lens_all[sharding.plan_shards(lens_all.astype(np.int64) + 1, world)[rank]])
+        else:
+            self.lens = lens_all
         self.max_seq = self.hi + 1
-        g = torch.Generator(device="cuda").manual_seed(seed)
+        g = torch.Generator(device="cuda").manual_seed(seed + rank)
         B, Hq, Hkv, D, S = self.B, self.Hq, self.Hkv, self.D, self.max_seq
         shape = (B, Hkv, S, D) if self.layout == b200attn.KV_HEAD_MAJOR else (B, S, Hkv, D)
         self.caches = []
@@ -477,7 +484,7 @@ def main():
     ctx = b200attn.Context(local)
     hbm, tflops, src = peaks()
 
-    w = DecodeWorkload(args.workload, 5 + rank, args.batch) if args.workload in ("c3", "c5") else \
+    w = DecodeWorkload(args.workload, 5, args.batch, world, rank) if args.workload in ("c3", "c5") else \
         PrefillWorkload(args.workload, {"c1": 1, "c2": 2, "c4": 4}[args.workload], args.batch)
     for _ in range(args.warmup):
         w.step(ctx)
@@ -537,10 +544,8 @@ def main():
         e2e_ms, h2d, d2h = elapsed_ms, 0, 0
 
     # max over ranks (device-timed)
-    t = torch.tensor([elapsed_ms, e2e_ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+    from b200attn import sharding
+    elapsed_ms, e2e_ms = sharding.max_over_ranks([elapsed_ms, e2e_ms])
     ms_step = elapsed_ms / args.steps
     tokens = w.tokens_per_step() * world
     value = tokens / (ms_step / 1e3)
