@@ -61,6 +61,11 @@ def test_plan_shards_is_balanced_and_covers_every_unit():
         sharding.plan_shards(np.ones(7, np.int64), 2)
 
 
+def test_max_over_ranks_without_a_process_group_is_the_identity():
+    from b200attn import sharding
+    assert sharding.max_over_ranks([3.5, 1.25]) == [3.5, 1.25]
+
+
 def test_two_gloo_ranks_reassemble_the_single_process_result():
     import torch.multiprocessing as mp
     world = 2

@@ -58,7 +58,8 @@ def max_over_ranks(values, group=None) -> list[float]:
     whole job is as slow as its slowest rank."""
     import torch
     import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:
+        return [float(v) for v in values]  # one process: nothing to reduce
     t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=_device_of(group))
-    if dist.is_initialized() and dist.get_world_size(group) > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return [float(x) for x in t.cpu()]
