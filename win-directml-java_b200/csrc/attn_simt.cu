@@ -17,6 +17,8 @@
 // scale folded in.  q/k arrive already rotated when RoPE applies.
 #include <math.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -24,12 +26,14 @@ namespace b2a {
 namespace {
 
 constexpr int kRows = 8;                     // query positions per CTA (one warp each)
-constexpr int kHeads = 8;                    // query heads per CTA (a GQA group, or a chunk of one)
+constexpr int kHeads = 8;                    // at most this many query heads per CTA (a GQA group or a chunk)
 constexpr int kTileKeys = 32;                // keys per shared-memory tile (one per lane)
-constexpr int kMaxPerLane = kMaxHeadDim / 32;
 
-__global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_constant__ AttnParams p, int G,
-                                                                int heads_here_max) {
+// kHT: query heads per CTA rounded up to 1, 2, 4 or 8; every K and V element read from
+// shared memory feeds all of them (independent FMA chains), padding heads are zeros.
+// kNPL: head dimensions per lane, ceil(D / 32) rounded up to 1, 2, 3, 4 or 8.
+template <int kHT, int kNPL>
+__global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_constant__ AttnParams p, int G) {
     extern __shared__ float sm[];
     const int D = p.D, Dp = D + 1;
     float* ks = sm;                          // [kTileKeys][D + 1]
@@ -45,13 +49,13 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
     const int s = s0 + warp;
     const bool row_valid = s < S;
 
-    // this row's query vectors, as fp32
-    for (int g = 0; g < nh; ++g)
+    // this row's query vectors, as fp32 (padding heads zero)
+    for (int g = 0; g < kHT; ++g)
         for (int d = lane; d < D; d += 32)
-            qs[(warp * heads_here_max + g) * D + d] =
-                row_valid ? load_as_float(p.q, b * p.q_sb + (int64_t)s * p.q_ss + (int64_t)(h0 + g) * p.q_sh + d,
-                                          p.in_dtype)
-                          : 0.f;
+            qs[(warp * kHT + g) * D + d] =
+                row_valid && g < nh
+                    ? load_as_float(p.q, b * p.q_sb + (int64_t)s * p.q_ss + (int64_t)(h0 + g) * p.q_sh + d, p.in_dtype)
+                    : 0.f;
 
     // visible keys of this row, and the CTA's union of them
     int first = 0, last = S - 1;
@@ -71,14 +75,14 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
         cta_first = p.window > 0 ? max(0, s0 - p.window + 1) : 0;
     }
     const float sl2 = p.scale * kLog2e;
-    float acc[kHeads][kMaxPerLane];
-    float m[kHeads], l[kHeads];
+    float acc[kHT][kNPL];
+    float m[kHT], l[kHT];
 #pragma unroll
-    for (int g = 0; g < kHeads; ++g) {
+    for (int g = 0; g < kHT; ++g) {
         m[g] = -INFINITY;
         l[g] = 0.f;
 #pragma unroll
-        for (int i = 0; i < kMaxPerLane; ++i) acc[g][i] = 0.f;
+        for (int i = 0; i < kNPL; ++i) acc[g][i] = 0.f;
     }
     const int64_t kbase = b * p.k_sb + (int64_t)kvh * p.k_sh;
     __syncthreads();
@@ -101,37 +105,71 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
         const bool vis = row_valid && j >= first && j <= last && j - kb < nk;
         const bool any = row_valid && kb <= last && kb + kTileKeys - 1 >= first;
         if (any) {
+            // scores of this lane's key for every head: one pass over the key row
+            float sc[kHT];
 #pragma unroll
-            for (int g = 0; g < kHeads; ++g) {
-                if (g >= nh) break;
-                float sc = -INFINITY;
-                if (vis) {
-                    if (uniform) {
-                        sc = 0.f;
-                    } else {
-                        const float* qg = qs + (warp * heads_here_max + g) * D;
-                        const float* kr = ks + lane * Dp;
-                        float dot = 0.f;
-                        for (int d = 0; d < D; ++d) dot = fmaf(qg[d], kr[d], dot);
-                        if (p.mask != nullptr) sc = (dot * p.scale + p.mask[(int64_t)b * S + j]) * kLog2e;
-                        else sc = dot * sl2;
+            for (int g = 0; g < kHT; ++g) sc[g] = -INFINITY;
+            if (vis) {
+                if (uniform) {
+#pragma unroll
+                    for (int g = 0; g < kHT; ++g) sc[g] = 0.f;
+                } else {
+                    const float* qw = qs + warp * kHT * D;
+                    const float* kr = ks + lane * Dp;
+                    float dot[kHT];
+#pragma unroll
+                    for (int g = 0; g < kHT; ++g) dot[g] = 0.f;
+                    // D is even and every q row starts 16-byte aligned when D % 4 == 0: q is read
+                    // four dimensions at a time (a broadcast), K one word at a time (odd row pitch)
+                    int d = 0;
+                    if ((D & 3) == 0) {
+#pragma unroll 2
+                        for (; d < D; d += 4) {
+                            const float k0 = kr[d], k1 = kr[d + 1], k2 = kr[d + 2], k3 = kr[d + 3];
+#pragma unroll
+                            for (int g = 0; g < kHT; ++g) {
+                                const float4 q4 = *reinterpret_cast<const float4*>(qw + g * D + d);
+                                dot[g] = fmaf(q4.x, k0, dot[g]);
+                                dot[g] = fmaf(q4.y, k1, dot[g]);
+                                dot[g] = fmaf(q4.z, k2, dot[g]);
+                                dot[g] = fmaf(q4.w, k3, dot[g]);
+                            }
+                        }
                     }
+                    for (; d < D; ++d) {
+                        const float kv = kr[d];
+#pragma unroll
+                        for (int g = 0; g < kHT; ++g) dot[g] = fmaf(qw[g * D + d], kv, dot[g]);
+                    }
+#pragma unroll
+                    for (int g = 0; g < kHT; ++g)
+                        sc[g] = p.mask != nullptr ? (dot[g] * p.scale + p.mask[(int64_t)b * S + j]) * kLog2e
+                                                  : dot[g] * sl2;
                 }
-                const float mn = fmaxf(m[g], warp_max(sc));
-                if (mn == -INFINITY) continue;  // nothing visible yet for this head (warp-uniform)
-                const float corr = exp2f(m[g] - mn);
-                const float pj = exp2f(sc - mn);
-                l[g] = l[g] * corr + warp_sum(pj);
+            }
+            float pj[kHT];
+#pragma unroll
+            for (int g = 0; g < kHT; ++g) {
+                const float mn = fmaxf(m[g], warp_max(sc[g]));
+                // mn is -inf only while nothing is visible (warp-uniform): keep the state
+                const float corr = mn == -INFINITY ? 1.f : fast_exp2(m[g] - mn);
+                pj[g] = mn == -INFINITY ? 0.f : fast_exp2(sc[g] - mn);
+                l[g] = l[g] * corr + warp_sum(pj[g]);
                 m[g] = mn;
 #pragma unroll
-                for (int i = 0; i < kMaxPerLane; ++i) acc[g][i] *= corr;
-                for (int jj = 0; jj < nk; ++jj) {
-                    const float pw = __shfl_sync(0xffffffffu, pj, jj);
+                for (int i = 0; i < kNPL; ++i) acc[g][i] *= corr;
+            }
+            for (int jj = 0; jj < nk; ++jj) {
+                float pw[kHT];
 #pragma unroll
-                    for (int i = 0; i < kMaxPerLane; ++i) {
-                        const int d = lane + 32 * i;
-                        if (d < D) acc[g][i] = fmaf(pw, vs[jj * Dp + d], acc[g][i]);
-                    }
+                for (int g = 0; g < kHT; ++g) pw[g] = __shfl_sync(0xffffffffu, pj[g], jj);
+#pragma unroll
+                for (int i = 0; i < kNPL; ++i) {
+                    // dimensions beyond D read the tile's padding (zeros or the next row): their
+                    // accumulators are never stored
+                    const float vv = vs[jj * Dp + min(lane + 32 * i, D)];
+#pragma unroll
+                    for (int g = 0; g < kHT; ++g) acc[g][i] = fmaf(pw[g], vv, acc[g][i]);
                 }
             }
         }
@@ -139,12 +177,12 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
     }
     if (!row_valid) return;
 #pragma unroll
-    for (int g = 0; g < kHeads; ++g) {
+    for (int g = 0; g < kHT; ++g) {
         if (g >= nh) break;
         const float inv = 1.f / l[g];
         const int64_t qo = b * p.q_sb + (int64_t)s * p.q_ss + (int64_t)(h0 + g) * p.q_sh;
 #pragma unroll
-        for (int i = 0; i < kMaxPerLane; ++i) {
+        for (int i = 0; i < kNPL; ++i) {
             const int d = lane + 32 * i;
             if (d < D) store_from_float(p.o, qo + d, acc[g][i] * inv, p.out_dtype);
         }
@@ -156,16 +194,33 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
 cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t stream) {
     const int G = p.Hq / p.Hkv;
     const int chunks = (G + kHeads - 1) / kHeads;
-    const int heads_here_max = G < kHeads ? G : kHeads;
-    const size_t smem = ((size_t)2 * kTileKeys * (p.D + 1) + (size_t)kRows * heads_here_max * p.D) * sizeof(float);
-    if (smem > 48 * 1024) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(attn_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
+    const int heads = G < kHeads ? G : kHeads;
+    const int ht = heads <= 1 ? 1 : heads <= 2 ? 2 : heads <= 4 ? 4 : 8;
+    const size_t smem = ((size_t)2 * kTileKeys * (p.D + 1) + (size_t)kRows * ht * p.D) * sizeof(float);
     const dim3 grid((p.S + kRows - 1) / kRows, p.Hkv * chunks, p.B);
-    attn_simt_kernel<<<grid, kRows * 32, smem, stream>>>(p, G, heads_here_max);
-    return cudaGetLastError();
+    auto go = [&](auto kernel) {
+        if (smem > 48 * 1024) {
+            const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+        }
+        kernel<<<grid, kRows * 32, smem, stream>>>(p, G);
+        return cudaGetLastError();
+    };
+    const int npl = (p.D + 31) / 32;
+    auto by_dims = [&](auto ht_tag) {
+        constexpr int HT = decltype(ht_tag)::value;
+        if (npl <= 1) return go(attn_simt_kernel<HT, 1>);
+        if (npl <= 2) return go(attn_simt_kernel<HT, 2>);
+        if (npl <= 3) return go(attn_simt_kernel<HT, 3>);
+        if (npl <= 4) return go(attn_simt_kernel<HT, 4>);
+        return go(attn_simt_kernel<HT, 8>);
+    };
+    switch (ht) {
+        case 1: return by_dims(std::integral_constant<int, 1>{});
+        case 2: return by_dims(std::integral_constant<int, 2>{});
+        case 4: return by_dims(std::integral_constant<int, 4>{});
+        default: return by_dims(std::integral_constant<int, 8>{});
+    }
 }
 
 }  // namespace b2a
