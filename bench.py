@@ -329,6 +329,29 @@ class PrefillWorkload:
                                     rope_theta=self.theta, stream=stream)
 
 
+def capture_graph(torch, fn):
+    """CUDA graph of fn(), which launches its work on the current stream (the library
+    calls take torch's current stream), or None when capture is not possible.  Replaying
+    it keeps Python and ctypes call overhead out of device-timed intervals: for kernels
+    of tens of microseconds a host-driven launch leaves the GPU idle between steps."""
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()  # warm on the capture's stream family: no first-use work inside the capture
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        torch.cuda.synchronize()
+        return g
+    except Exception as e:  # report and time direct launches instead
+        print(f"# CUDA graph capture failed ({type(e).__name__}: {e}); timing direct launches", file=sys.stderr)
+        torch.cuda.synchronize()
+        return None
+
+
 def time_steps(torch, fn, steps, flush=None):
     """Per-step CUDA-event durations (ms) on the current stream."""
     s = torch.cuda.current_stream()
@@ -353,7 +376,12 @@ def run_suite(ctx, hbm, tflops, src):
         for _ in range(3):
             w.step(ctx)
         torch.cuda.synchronize()
-        ms = statistics.mean(time_steps(torch, lambda: w.step(ctx), 10, flush))
+        # one step as a CUDA graph, captured after this workload's warm-up (the context's
+        # workspaces have their final size) and dropped before the next workload runs
+        g = capture_graph(torch, lambda: w.step(ctx))
+        ms = statistics.mean(time_steps(torch, (lambda: g.replay()) if g is not None else (lambda: w.step(ctx)),
+                                        10, flush))
+        del g
         entry = {"workload": WORKLOADS[name], "ms": round(ms, 4),
                  "tokens_per_s": round(w.tokens_per_step() / (ms / 1e3), 1)}
         gbs = w.algorithmic_bytes() / (ms / 1e3) / 1e9
@@ -495,7 +523,15 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    # ---- device-resident timed region
+    # ---- device-resident timed region: CUDA graph replays of the same launches
+    # (one graph per decode layer, one per prefill step), captured after warm-up
+    if isinstance(w, DecodeWorkload):
+        graphs = [capture_graph(torch, (lambda i=i: w.launch(ctx, i))) for i in range(len(w.layers))]
+        run_layer = [(g.replay if g is not None else (lambda i=i: w.launch(ctx, i))) for i, g in enumerate(graphs)]
+    else:
+        graphs = [capture_graph(torch, lambda: w.step(ctx))]
+        run_step = graphs[0].replay if graphs[0] is not None else (lambda: w.step(ctx))
+    launch_mode = "CUDA graph replay" if all(g is not None for g in graphs) else "direct launches"
     s = torch.cuda.current_stream()
     per_launch = []
     barrier()
@@ -509,7 +545,7 @@ def main():
                 for i in range(len(w.layers)):
                     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     a.record(s)
-                    w.launch(ctx, i)
+                    run_layer[i]()
                     b.record(s)
                     evs.append((a, b))
         else:
@@ -517,7 +553,7 @@ def main():
             for _ in range(args.steps):
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(s)
-                w.step(ctx)
+                run_step()
                 b.record(s)
                 evs.append((a, b))
         t1.record(s)
@@ -525,6 +561,7 @@ def main():
     elapsed_ms = t0.elapsed_time(t1)
     per_launch = [a.elapsed_time(b) for a, b in evs]
     clocks = clk.summary() or clk_smi.summary()
+    del graphs
 
     # ---- end-to-end timed region (host buffers, copies inside)
     if isinstance(w, DecodeWorkload):
@@ -578,7 +615,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16" if isinstance(w, DecodeWorkload) else str(w.dt).split(".")[-1],
             "data": "synthetic (seeded N(0,1); no dataset or checkpoint)",
-            "config": dict({"workload": WORKLOADS[args.workload], "parallelism": f"shard{world} (sequences per rank)"},
+            "config": dict({"workload": WORKLOADS[args.workload], "parallelism": f"shard{world} (sequences per rank)",
+                            "launch": launch_mode},
                            **(w.config() if isinstance(w, DecodeWorkload) else {})),
             "roofline": roof,
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,

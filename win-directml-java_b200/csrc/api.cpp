@@ -147,9 +147,10 @@ int run_decode(b2a_context* ctx, DecodeParams& p, cudaStream_t stream, bool allo
         p.target_items = target;
         p.item_capacity = cap;
         const int B = p.B;
-        // one launch covers at most kDecodeMaxBatchPerLaunch sequences and
-        // fewer than 2^31 visible keys (the kernel's int32 prefix)
-        const int per_launch = (int)std::min<int64_t>(kDecodeMaxBatchPerLaunch, INT32_MAX / ((int64_t)p.max_seq + 1));
+        // one launch covers at most kDecodeMaxBatchPerLaunch sequences and a key
+        // stream (visible keys plus per-unit overhead keys) below 2^31 (the kernel's int32 prefix)
+        const int per_launch = (int)std::min<int64_t>(kDecodeMaxBatchPerLaunch,
+                                                      INT32_MAX / ((int64_t)p.max_seq + 1 + kDecodeGapKeysMax));
         for (int b0 = 0; b0 < B; b0 += per_launch) {
             DecodeParams s = p;
             s.B = std::min(per_launch, B - b0);

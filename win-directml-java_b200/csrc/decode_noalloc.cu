@@ -103,9 +103,10 @@ extern "C" B2A_API int b2a_decode_noalloc(int q_dtype, int cache_dtype, int out_
     if (B > kDecodeMaxBatchPerLaunch || units > kMaxUnits)
         return reject(B2A_EINVAL, "b2a_decode_noalloc: batch x kv heads x ceil(G/8) = %lld exceeds the static "
                                   "scratch limit of %lld units (batch <= 2048)", units, kMaxUnits);
-    if ((long long)B * ((long long)max_seq + 1) >= INT32_MAX)
-        return reject(B2A_EINVAL, "b2a_decode_noalloc: batch x max_seq = %lld must stay below %lld",
-                      (long long)B * max_seq, INT32_MAX);
+    static_assert(kDecodeGapKeysMax == 640, "the message below names max_seq + 641");
+    if ((long long)B * ((long long)max_seq + 1 + kDecodeGapKeysMax) >= INT32_MAX)
+        return reject(B2A_EINVAL, "b2a_decode_noalloc: batch x (max_seq + 641) = %lld must stay below %lld",
+                      (long long)B * ((long long)max_seq + 1 + kDecodeGapKeysMax), INT32_MAX);
 
     int device = 0;
     cudaError_t e = cudaGetDevice(&device);

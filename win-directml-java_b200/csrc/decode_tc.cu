@@ -52,6 +52,12 @@ template <int D>
 struct Geo {
     static constexpr int kRow = D + 8;  // padded smem row (elements): odd number of 16 B units
     static constexpr int kStages = D <= 64 ? 4 : 3;
+    // Fixed cost of one piece (tile issue, q prologue, epilogue and merge) in keys of
+    // streaming time, measured on B200 with in-kernel timers: ~6 us per piece against
+    // ~0.6 us per 64-key tile at D = 64, relatively less at larger D.  The stream-K
+    // split charges it to every unit, so CTAs that cross unit boundaries take fewer keys.
+    static constexpr int kGapKeys = D <= 64 ? 640 : (D <= 128 ? 384 : 256);
+    static_assert(kGapKeys <= kDecodeGapKeysMax, "host launch split assumes this bound");
     static constexpr int kStageElems = 2 * kTile * kRow;  // K tile then V tile
     static constexpr int kChunks = D / 8;                 // 16-byte chunks per cache row
     static constexpr size_t kPipeBytes = size_t(kStages) * kStageElems * 2;
@@ -190,11 +196,13 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
 
     // ---------------------------------------------------------------- plan
     // Stream-K split: the visible keys of all units (sequence, kv head, head
-    // group) form one key stream; CTA c owns the contiguous range
-    // [c*R, (c+1)*R), R = ceil(total / gridDim.x).  Work is balanced to one
-    // key, and a unit is cut only where CTA ranges cross it.
-    // prefix[b] = visible keys of sequences < b (int32: the host keeps each
-    // launch's total below 2^31).
+    // group), each followed by kGapKeys keys that stand for its fixed per-piece
+    // cost, form one key stream; CTA c owns the contiguous range
+    // [c*R, (c+1)*R), R = ceil(total / gridDim.x).  Work is balanced to about a
+    // tile, and a unit is cut only where CTA ranges cross its real keys; a range
+    // that falls on a unit's gap does no work there.
+    // prefix[b] = stream length of sequences < b, per unit (int32: the host keeps
+    // each launch's total below 2^31).
     {
         const int per = (p.B + kThreads - 1) / kThreads;
         const int b0 = min(p.B, tid * per), b1 = min(p.B, b0 + per);
@@ -202,7 +210,7 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         for (int b = b0; b < b1; ++b) {
             int L, first;
             if (!seq_range(p, b, L, first)) bad = 1;
-            run += L - first + 1;
+            run += L - first + 1 + Gm::kGapKeys;
         }
         if (bad && blockIdx.x == 0) atomicOr(p.status, 1);
         int incl = run;
@@ -220,7 +228,7 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
             prefix[b] = acc;
             int L, first;
             seq_range(p, b, L, first);
-            acc += L - first + 1;
+            acc += L - first + 1 + Gm::kGapKeys;
         }
         if (tid == kThreads - 1) prefix[p.B] = warp_off + incl;
         __syncthreads();
@@ -249,9 +257,14 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         int L, first;
         const bool ok = seq_range(p, b, L, first);
         const int n_b = L - first + 1;
+        const int n_v = n_b + Gm::kGapKeys;  // the unit's stream length
         const long long seq_base = (long long)prefix[b] * per_chunk;
-        const int r = (int)((pos - seq_base) / n_b);
-        const long long u_start = seq_base + (long long)r * n_b, u_end = u_start + n_b;
+        const int r = (int)((pos - seq_base) / n_v);
+        const long long u_start = seq_base + (long long)r * n_v, u_end = u_start + n_b;
+        if (pos >= u_end) {  // in the unit's gap: nothing to attend
+            pos = u_start + n_v;
+            continue;
+        }
         const long long piece_end = min(range_hi, u_end);
         const int kvh = r / p.n_hg, hg = r - kvh * p.n_hg;
         const int k0 = first + (int)(pos - u_start);

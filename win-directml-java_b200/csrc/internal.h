@@ -9,6 +9,9 @@ namespace b2a {
 
 constexpr int kMaxHeadDim = 256;
 constexpr int kDecodeMaxBatchPerLaunch = 2048;
+// Largest per-unit overhead (in keys) the decode split adds to each unit's stream
+// length; launches keep B * (max_seq + 1 + kDecodeGapKeysMax) below 2^31.
+constexpr int kDecodeGapKeysMax = 640;
 
 // One decode step (or one attention over an existing cache when append == 0).
 struct DecodeParams {
