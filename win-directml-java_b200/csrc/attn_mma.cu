@@ -41,7 +41,12 @@ __global__ void __launch_bounds__(kThreads) attn_mma_kernel(const __grid_constan
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int n_mt = (p.S + kBM - 1) / kBM;
+    // parameter fields in registers: the asm statements below (cp.async, ldmatrix) clobber
+    // memory, which would otherwise reload each field through a generic pointer at every use
+    const int S = p.S, causal = p.causal, window = p.window;
+    const float* const mask = p.mask;
+    const float scale = p.scale;
+    const int n_mt = (S + kBM - 1) / kBM;
     const int mt_idx = n_mt - 1 - (int)blockIdx.x;  // heavy causal tiles first
     const int h = blockIdx.y, b = blockIdx.z;
     const int kvh = h / (p.Hq / p.Hkv);
@@ -52,16 +57,16 @@ __global__ void __launch_bounds__(kThreads) attn_mma_kernel(const __grid_constan
     const T* vg = static_cast<const T*>(p.v) + b * p.k_sb + kvh * p.k_sh;
 
     // key range for this query tile
-    int key_end = p.S;  // exclusive
+    int key_end = S;  // exclusive
     int key_begin = 0;
     bool uniform = false;
-    if (p.causal) {
-        key_end = min(p.S, m0 + kBM);
-        if (p.window > 0) key_begin = max(0, m0 - p.window + 1);
+    if (causal) {
+        key_end = min(S, m0 + kBM);
+        if (window > 0) key_begin = max(0, m0 - window + 1);
     } else if (p.key_len != nullptr) {
         const int kl = p.key_len[b];
         if (kl <= 0) uniform = true;
-        else key_end = min(kl, p.S);
+        else key_end = min(kl, S);
     }
     const int t_begin = key_begin / kBN;
     const int n_tiles = (key_end + kBN - 1) / kBN - t_begin;
@@ -78,11 +83,11 @@ __global__ void __launch_bounds__(kThreads) attn_mma_kernel(const __grid_constan
     auto load_kv = [&](int tile, int stage) {
         const int n0 = (t_begin + tile) * kBN;
         T* ks = kv_s + (2 * stage) * kBM * kRow;
-        load_rows(ks, kg, p.k_ss, n0, p.S);
-        load_rows(ks + kBM * kRow, vg, p.k_ss, n0, p.S);
+        load_rows(ks, kg, p.k_ss, n0, S);
+        load_rows(ks + kBM * kRow, vg, p.k_ss, n0, S);
     };
 
-    load_rows(q_s, qg, p.q_ss, m0, p.S);
+    load_rows(q_s, qg, p.q_ss, m0, S);
     if (n_tiles > 0) load_kv(0, 0);
     cp_async_commit();
 
@@ -91,7 +96,7 @@ __global__ void __launch_bounds__(kThreads) attn_mma_kernel(const __grid_constan
 #pragma unroll
     for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float mr0 = -INFINITY, mr1 = -INFINITY, lr0 = 0.f, lr1 = 0.f;
-    const float sl2 = p.scale * kLog2e;
+    const float sl2 = scale * kLog2e;
     const int qrow0 = m0 + warp * 16 + g, qrow1 = qrow0 + 8;
 
     for (int tile = 0; tile < n_tiles; ++tile) {
@@ -128,25 +133,39 @@ __global__ void __launch_bounds__(kThreads) attn_mma_kernel(const __grid_constan
                 Mma<T>::run(s[2 * np + 1], qa[ks], bf[2], bf[3]);
             }
         }
-        // scale + mask, row max
+        // scale + mask, row max; tiles every key of which this warp's 16 rows see take the
+        // scale alone
+        const int wq0 = m0 + warp * 16;
+        const bool edge = uniform || mask != nullptr || n0 < key_begin || n0 + kBN > key_end ||
+                          (causal && n0 + kBN - 1 > wq0) || (causal && window > 0 && n0 <= wq0 + 15 - window);
         float mx0 = -INFINITY, mx1 = -INFINITY;
+        if (!edge) {
 #pragma unroll
-        for (int nt = 0; nt < kBN / 8; ++nt) {
+            for (int nt = 0; nt < kBN / 8; ++nt) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int kj = n0 + nt * 8 + 2 * t + (e & 1);
-                const int qi = (e < 2) ? qrow0 : qrow1;
-                bool vis = kj < key_end && kj >= key_begin;
-                if (p.causal) vis = vis && kj <= qi && (p.window <= 0 || kj > qi - p.window);
-                float v;
-                if (!vis) v = -INFINITY;
-                else if (uniform) v = 0.f;
-                else if (p.mask != nullptr) v = (s[nt][e] * p.scale + p.mask[(int64_t)b * p.S + kj]) * kLog2e;
-                else v = s[nt][e] * sl2;
-                s[nt][e] = v;
+                for (int e = 0; e < 4; ++e) s[nt][e] *= sl2;
+                mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
+                mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
             }
-            mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
-            mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
+        } else {
+#pragma unroll
+            for (int nt = 0; nt < kBN / 8; ++nt) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int kj = n0 + nt * 8 + 2 * t + (e & 1);
+                    const int qi = (e < 2) ? qrow0 : qrow1;
+                    bool vis = kj < key_end && kj >= key_begin;
+                    if (causal) vis = vis && kj <= qi && (window <= 0 || kj > qi - window);
+                    float v;
+                    if (!vis) v = -INFINITY;
+                    else if (uniform) v = 0.f;
+                    else if (mask != nullptr) v = (s[nt][e] * scale + mask[(int64_t)b * S + kj]) * kLog2e;
+                    else v = s[nt][e] * sl2;
+                    s[nt][e] = v;
+                }
+                mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
+                mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
+            }
         }
 #pragma unroll
         for (int off = 1; off < 4; off <<= 1) {
@@ -207,12 +226,12 @@ __global__ void __launch_bounds__(kThreads) attn_mma_kernel(const __grid_constan
 #pragma unroll
     for (int dt = 0; dt < D / 8; ++dt) {
         const int d = dt * 8 + 2 * t;
-        if (qrow0 < p.S) {
+        if (qrow0 < S) {
             const int64_t off = b * p.q_sb + (int64_t)qrow0 * p.q_ss + h * p.q_sh + d;
             store_from_float(p.o, off, o[dt][0] * i0, p.out_dtype);
             store_from_float(p.o, off + 1, o[dt][1] * i0, p.out_dtype);
         }
-        if (qrow1 < p.S) {
+        if (qrow1 < S) {
             const int64_t off = b * p.q_sb + (int64_t)qrow1 * p.q_ss + h * p.q_sh + d;
             store_from_float(p.o, off, o[dt][2] * i1, p.out_dtype);
             store_from_float(p.o, off + 1, o[dt][3] * i1, p.out_dtype);
