@@ -237,6 +237,20 @@ B2A_API int b2a_qwen_rope_and_append(b2a_context* ctx, float* q, const float* k,
                                      int head_dim, int pos, int max_seq_len, float rope_theta,
                                      void* stream);
 
+/* One Qwen2 decode-layer attention step on the fused QKV projection output, in one
+ * launch: QwenGpuPipeline.decodeLayerGpuResident steps 1b-3
+ * (INF/qwen/QwenGpuPipeline.java:647-691), which dispatch the fused-bias Add,
+ * ROPE_AND_APPEND_HLSL and GQA_ATTENTION_DECODE_HLSL.  qkv is one token's
+ * [Q (numHeads*headDim) | K (kvHeads*headDim) | V (kvHeads*headDim)] row;
+ * qkv_bias (same layout, or NULL) is added first; q and k are rotated at pos
+ * (angles in double, as b2a_qwen_rope_and_append); k and v are written into the
+ * float caches [kvHeads][maxSeqLen][headDim] at pos; attn_out [numHeads*headDim]
+ * = softmax(scale * q.K[0..pos]) . V.  All float32.  qkv is not modified (the
+ * reference rotates Q in place as an intermediate nothing reads afterwards). */
+B2A_API int b2a_qwen_decode_step(b2a_context* ctx, const float* qkv, const float* qkv_bias, float* k_cache,
+                                 float* v_cache, float* attn_out, int num_heads, int kv_heads, int head_dim, int pos,
+                                 int max_seq_len, float rope_theta, float scale, void* stream);
+
 /* GQA_ATTENTION_DECODE_HLSL (WB/windows/QwenAttentionShaders.java:168-263), root
  * constants {numHeads, kvHeads, headDim, qHeadsPerKvHead, seqLen, maxSeqLen, scale}:
  * attn_out[h] = softmax(scale * q[h].K[0..seqLen)) . V over the float caches

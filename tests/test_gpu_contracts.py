@@ -73,6 +73,52 @@ def test_qwen_gqa_attention_decode_matches_cpu_reference(ctx):
     np.testing.assert_allclose(out.cpu().numpy(), want.ravel(), atol=TOL)
 
 
+@pytest.mark.parametrize("num_heads,kv_heads,head_dim,max_seq,pos,bias,seed", [
+    (NUM_HEADS, KV_HEADS, HEAD_DIM, MAX_SEQ, 2, True, 42),   # the shader test shapes, fused
+    (14, 2, 64, 128, 77, True, 7),                           # a Qwen2.5-0.5B layer
+    (14, 2, 64, 128, 0, False, 8),                           # first token, no bias
+])
+def test_qwen_decode_step_fused_matches_oracle(ctx, num_heads, kv_heads, head_dim, max_seq, pos, bias, seed):
+    """b2a_qwen_decode_step = QwenGpuPipeline.decodeLayerGpuResident steps 1b-3 (fused bias Add,
+    ROPE_AND_APPEND, GQA_ATTENTION_DECODE) on one fused [Q|K|V] row: the output within the shader
+    tests' 1e-4, the appended rows within one float ulp, every other cache row untouched."""
+    import torch
+    import b200attn
+    rng = oracle.JavaRandom(seed)
+    q_size, kv_size = num_heads * head_dim, kv_heads * head_dim
+    qkv = rng.floats_pm1(q_size + 2 * kv_size)
+    qkv_bias = rng.floats_pm1(q_size + 2 * kv_size, 0.25) if bias else None
+    kc = rng.floats_pm1(kv_heads * max_seq * head_dim)
+    vc = rng.floats_pm1(kv_heads * max_seq * head_dim)
+    scale = float(np.float32(1.0 / math.sqrt(head_dim)))
+    theta = 1000000.0
+    x = qkv + qkv_bias if bias else qkv.copy()  # the Add dispatch, in float32
+    want, kc_want, vc_want = oracle.decode(
+        x[:q_size].reshape(1, num_heads, head_dim), x[q_size:q_size + kv_size].reshape(1, kv_heads, head_dim),
+        x[q_size + kv_size:].reshape(1, kv_heads, head_dim), kc.reshape(1, kv_heads, max_seq, head_dim),
+        vc.reshape(1, kv_heads, max_seq, head_dim), [pos], B=1, Hq=num_heads, Hkv=kv_heads, D=head_dim,
+        max_seq=max_seq, scale=scale, rope_theta=theta, rope_mode=oracle.ROPE_DECODERONLY,
+        cache_layout=oracle.KV_HEAD_MAJOR, cache_dtype=oracle.F32)
+    kcd, vcd = _dev(kc), _dev(vc)
+    qkvd = _dev(qkv)
+    out = torch.zeros(q_size, device="cuda")
+    b200attn.QwenAttentionShaders(ctx).decode_step(qkvd, _dev(qkv_bias) if bias else None, kcd, vcd, out, num_heads,
+                                                   kv_heads, head_dim, pos, max_seq, theta, scale)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out.cpu().numpy(), want.ravel(), atol=TOL)
+    np.testing.assert_array_equal(qkvd.cpu().numpy(), qkv)  # the input row is not modified
+    got_k, got_v = kcd.cpu().numpy(), vcd.cpu().numpy()
+    kw, vw = kc_want.ravel(), vc_want.ravel()
+    rows = np.zeros((kv_heads, max_seq), bool)
+    rows[:, pos] = True
+    rows = np.repeat(rows.ravel(), head_dim)
+    np.testing.assert_array_equal(got_k[~rows], kc[~rows])
+    np.testing.assert_array_equal(got_v[~rows], vc[~rows])
+    ulp = np.spacing(np.abs(kw[rows]).astype(np.float32))
+    assert np.all(np.abs(got_k[rows] - kw[rows]) <= ulp)
+    np.testing.assert_array_equal(got_v[rows], vw[rows])
+
+
 @pytest.mark.parametrize("num_heads,num_kv,head_dim,seq_len,first_valid,seed", [
     (4, 1, 256, 6, 0, 1),   # Gemma 270M shape, full attention
     (4, 1, 256, 12, 7, 2),  # local layer: firstValid > 0

@@ -100,11 +100,12 @@ def lib() -> ctypes.CDLL:
                                  _i, _vp, _vp, _f, _vp, _vp]
         L.b2a_qwen_rope_and_append.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp]
         L.b2a_qwen_gqa_attention_decode.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp]
+        L.b2a_qwen_decode_step.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _f, _vp]
         L.b2a_gemma_fused_attention_context.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp]
         L.b2a_partition_units.argtypes = [_i, _i, _vp, _vp]
         for name in ("b2a_create", "b2a_destroy", "b2a_last_error", "b2a_set_workspace_limit", "b2a_workspace_bytes",
                      "b2a_reserve_decode", "b2a_check_device_status", "b2a_mha", "b2a_prefill_causal", "b2a_decode",
-                     "b2a_qwen_rope_and_append", "b2a_qwen_gqa_attention_decode",
+                     "b2a_qwen_rope_and_append", "b2a_qwen_gqa_attention_decode", "b2a_qwen_decode_step",
                      "b2a_gemma_fused_attention_context", "b2a_partition_units"):
             getattr(L, name).restype = _i
         _lib = L
@@ -332,6 +333,14 @@ class QwenAttentionShaders:
                                                            _ptr(attn_out), num_heads, kv_heads, head_dim,
                                                            q_heads_per_kv_head, seq_len, max_seq_len, scale,
                                                            _stream(stream)))
+
+    def decode_step(self, qkv, qkv_bias, k_cache, v_cache, attn_out, num_heads, kv_heads, head_dim, pos, max_seq_len,
+                    rope_theta, scale, stream=None):
+        """Bias + RoPE + KV append + GQA attention of one token from the fused [Q|K|V] row
+        (QwenGpuPipeline.decodeLayerGpuResident steps 1b-3) in one launch."""
+        self.ctx.check(lib().b2a_qwen_decode_step(self.ctx.handle, _ptr(qkv), _ptr(qkv_bias), _ptr(k_cache),
+                                                  _ptr(v_cache), _ptr(attn_out), num_heads, kv_heads, head_dim, pos,
+                                                  max_seq_len, rope_theta, scale, _stream(stream)))
 
 
 class Gemma3FusedAttentionContext:

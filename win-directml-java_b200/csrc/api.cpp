@@ -155,9 +155,9 @@ int run_decode(b2a_context* ctx, DecodeParams& p, cudaStream_t stream, bool allo
             DecodeParams s = p;
             s.B = std::min(per_launch, B - b0);
             const size_t qe = dtype_size(p.q_dtype), oe = dtype_size(p.out_dtype), ce = dtype_size(p.cache_dtype);
-            s.q = static_cast<const char*>(p.q) + (size_t)b0 * p.Hq * p.D * qe;
-            if (p.k_new) s.k_new = static_cast<const char*>(p.k_new) + (size_t)b0 * p.Hkv * p.D * qe;
-            if (p.v_new) s.v_new = static_cast<const char*>(p.v_new) + (size_t)b0 * p.Hkv * p.D * qe;
+            s.q = static_cast<const char*>(p.q) + (size_t)b0 * q_stride_of(p) * qe;
+            if (p.k_new) s.k_new = static_cast<const char*>(p.k_new) + (size_t)b0 * kvn_stride_of(p) * qe;
+            if (p.v_new) s.v_new = static_cast<const char*>(p.v_new) + (size_t)b0 * kvn_stride_of(p) * qe;
             s.k_cache = static_cast<char*>(p.k_cache) + (size_t)b0 * p.stride_b * ce;
             s.v_cache = static_cast<char*>(p.v_cache) + (size_t)b0 * p.stride_b * ce;
             if (p.ctx_lens) s.ctx_lens = p.ctx_lens + b0;
@@ -622,6 +622,58 @@ B2A_API int b2a_qwen_gqa_attention_decode(b2a_context* ctx, const float* q, cons
     p.max_seq = max_seq_len;
     p.first_explicit = 0;
     p.append = 0;
+    p.scale = scale;
+    p.out = attn_out;
+    p.out_dtype = B2A_FLOAT32;
+    return run_decode(ctx, p, static_cast<cudaStream_t>(stream), false);
+}
+
+B2A_API int b2a_qwen_decode_step(b2a_context* ctx, const float* qkv, const float* qkv_bias, float* k_cache,
+                                 float* v_cache, float* attn_out, int num_heads, int kv_heads, int head_dim, int pos,
+                                 int max_seq_len, float rope_theta, float scale, void* stream) {
+    // QwenGpuPipeline.decodeLayerGpuResident steps 1b-3 in one launch
+    // (INF/qwen/QwenGpuPipeline.java:647-691): bias add on the fused [Q|K|V] row, RoPE of q and k
+    // at pos, k/v append at pos, GQA attention over cache positions [0, pos].
+    if (!ctx) return B2A_EINVAL;
+    if (!qkv || !k_cache || !v_cache || !attn_out)
+        return fail(ctx, B2A_EINVAL, "qkv, caches and attn_out must not be null");
+    int rc = check_heads(ctx, num_heads, kv_heads);
+    if (rc) return rc;
+    if ((rc = check_head_dim(ctx, head_dim))) return rc;
+    if (pos < 0 || pos >= max_seq_len) return fail(ctx, B2A_EINVAL, "pos %d outside [0, maxSeqLen=%d)", pos, max_seq_len);
+    if (!(rope_theta > 0.f)) return fail(ctx, B2A_EINVAL, "rope theta must be > 0");
+    if (!(scale == scale) || scale <= 0.f) return fail(ctx, B2A_EINVAL, "scale must be a positive number");
+    DeviceGuard guard(ctx->device);
+    const int64_t q_size = (int64_t)num_heads * head_dim, kv_size = (int64_t)kv_heads * head_dim;
+    DecodeParams p{};
+    p.q = qkv;
+    p.k_new = qkv + q_size;
+    p.v_new = qkv + q_size + kv_size;
+    p.q_dtype = B2A_FLOAT32;
+    p.q_seq_stride = p.kv_new_seq_stride = q_size + 2 * kv_size;
+    if (qkv_bias) {
+        p.q_bias = qkv_bias;
+        p.k_bias = qkv_bias + q_size;
+        p.v_bias = qkv_bias + q_size + kv_size;
+    }
+    p.k_cache = k_cache;
+    p.v_cache = v_cache;
+    p.cache_dtype = B2A_FLOAT32;
+    p.stride_b = 0;
+    p.stride_h = (int64_t)max_seq_len * head_dim;
+    p.stride_pos = head_dim;
+    p.ctx_lens = nullptr;
+    p.pos_scalar = pos;
+    p.B = 1;
+    p.Hq = num_heads;
+    p.Hkv = kv_heads;
+    p.G = num_heads / kv_heads;
+    p.D = head_dim;
+    p.max_seq = max_seq_len;
+    p.first_explicit = 0;
+    p.append = 1;
+    p.rope_mode = B2A_ROPE_NEOX;
+    inv_freq_table((double)rope_theta, head_dim, p.inv_freq);
     p.scale = scale;
     p.out = attn_out;
     p.out_dtype = B2A_FLOAT32;

@@ -41,11 +41,12 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 
 // Norm + RoPE of one head vector into vec[0..D) (float), whole warp.
 __device__ void prep_head_generic(const DecodeParams& p, const void* src, int64_t off, int dtype,
-                                  const float* norm_w, bool rope, int L, float* vec, int lane) {
+                                  const float* bias, const float* norm_w, bool rope, int L, float* vec, int lane) {
     const int D = p.D;
     double ss = 0.0;
     for (int d = lane; d < D; d += 32) {
-        const float x = load_as_float(src, off + d, dtype);
+        float x = load_as_float(src, off + d, dtype);
+        if (bias != nullptr) x = __fadd_rn(x, bias[d]);  // projection bias, fp32
         vec[d] = x;
         ss += (double)x * (double)x;
     }
@@ -98,15 +99,17 @@ __global__ void __launch_bounds__(kWarps * 32) decode_simt_kernel(const __grid_c
         return;
     }
     const bool rope = p.append && p.rope_mode != 0;
-    prep_head_generic(p, p.q, ((int64_t)b * p.Hq + h) * D, p.q_dtype, p.append ? p.q_norm_w : nullptr, rope, L, qv,
-                      lane);
+    prep_head_generic(p, p.q, (int64_t)b * q_stride_of(p) + (int64_t)h * D, p.q_dtype,
+                      p.q_bias ? p.q_bias + h * D : nullptr, p.append ? p.q_norm_w : nullptr, rope, L, qv, lane);
     const int64_t row0 = b * p.stride_b + kvh * p.stride_h;
     if (p.append) {
-        prep_head_generic(p, p.k_new, ((int64_t)b * p.Hkv + kvh) * D, p.q_dtype, p.k_norm_w, rope, L, kn, lane);
+        prep_head_generic(p, p.k_new, (int64_t)b * kvn_stride_of(p) + (int64_t)kvh * D, p.q_dtype,
+                          p.k_bias ? p.k_bias + kvh * D : nullptr, p.k_norm_w, rope, L, kn, lane);
         for (int d = lane; d < D; d += 32) {
             kn[d] = round_through(kn[d], p.cache_dtype);
-            vn[d] = round_through(load_as_float(p.v_new, ((int64_t)b * p.Hkv + kvh) * D + d, p.q_dtype),
-                                  p.cache_dtype);
+            float vf = load_as_float(p.v_new, (int64_t)b * kvn_stride_of(p) + (int64_t)kvh * D + d, p.q_dtype);
+            if (p.v_bias != nullptr) vf = __fadd_rn(vf, p.v_bias[kvh * D + d]);
+            vn[d] = round_through(vf, p.cache_dtype);
             if (h % p.G == 0) {  // one writer per kv head; readers use kn/vn for row L
                 store_from_float(p.k_cache, row0 + (int64_t)L * p.stride_pos + d, kn[d], p.cache_dtype);
                 store_from_float(p.v_cache, row0 + (int64_t)L * p.stride_pos + d, vn[d], p.cache_dtype);

@@ -110,13 +110,14 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 // when requested) as float into vec[0..D).  Whole warp; vec is warp-private.
 template <int D>
 __device__ __forceinline__ void prep_head(const DecodeParams& p, const void* src, int64_t off, int dtype,
-                                          const float* norm_w, bool rope, const double* cs, float* vec,
-                                          int lane) {
+                                          const float* bias, const float* norm_w, bool rope, const double* cs,
+                                          float* vec, int lane) {
     double ss = 0.0;
     float x[D / 32];
 #pragma unroll
     for (int j = 0; j < D / 32; ++j) {
         x[j] = load_as_float(src, off + lane + 32 * j, dtype);
+        if (bias != nullptr) x[j] = __fadd_rn(x[j], bias[lane + 32 * j]);  // projection bias, fp32
         ss += (double)x[j] * (double)x[j];
     }
     if (norm_w != nullptr) {
@@ -327,8 +328,9 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
                 for (int d = lane; d < D; d += 32) qrow[d] = qlo[d] = Elem<T>::from_float(0.f);
                 continue;
             }
-            prep_head<D>(p, p.q, ((int64_t)b * p.Hq + h0 + hl) * D, p.q_dtype, p.append ? p.q_norm_w : nullptr,
-                         rope, cs_s, vec, lane);
+            prep_head<D>(p, p.q, (int64_t)b * q_stride_of(p) + (int64_t)(h0 + hl) * D, p.q_dtype,
+                         p.q_bias ? p.q_bias + (h0 + hl) * D : nullptr, p.append ? p.q_norm_w : nullptr, rope, cs_s,
+                         vec, lane);
             for (int d = lane; d < D; d += 32) {
                 const T hi = Elem<T>::from_float(vec[d]);
                 qrow[d] = hi;
@@ -338,8 +340,8 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         }
         if (has_new) {
             if (warp == 0) {
-                prep_head<D>(p, p.k_new, ((int64_t)b * p.Hkv + kvh) * D, p.q_dtype, p.k_norm_w, rope, cs_s, vec,
-                             lane);
+                prep_head<D>(p, p.k_new, (int64_t)b * kvn_stride_of(p) + (int64_t)kvh * D, p.q_dtype,
+                             p.k_bias ? p.k_bias + kvh * D : nullptr, p.k_norm_w, rope, cs_s, vec, lane);
                 T* dst = static_cast<T*>(p.k_cache) + b * p.stride_b + kvh * p.stride_h + (int64_t)L * p.stride_pos;
                 for (int d = lane; d < D; d += 32) {
                     const T v = Elem<T>::from_float(vec[d]);
@@ -349,7 +351,9 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
             } else if (warp == 1) {
                 T* dst = static_cast<T*>(p.v_cache) + b * p.stride_b + kvh * p.stride_h + (int64_t)L * p.stride_pos;
                 for (int d = lane; d < D; d += 32) {
-                    const T v = Elem<T>::from_float(load_as_float(p.v_new, ((int64_t)b * p.Hkv + kvh) * D + d, p.q_dtype));
+                    float vf = load_as_float(p.v_new, (int64_t)b * kvn_stride_of(p) + (int64_t)kvh * D + d, p.q_dtype);
+                    if (p.v_bias != nullptr) vf = __fadd_rn(vf, p.v_bias[kvh * D + d]);
+                    const T v = Elem<T>::from_float(vf);
                     vnew_s[d] = v;
                     if (hg == 0) dst[d] = v;
                 }

@@ -44,8 +44,21 @@ struct DecodeParams {
     int n_hg;            // head groups of 8 per kv head
     int target_items;
     int item_capacity;
+    // per-sequence element strides of q and of the new k/v rows; 0 means contiguous
+    // (Hq * D and Hkv * D).  A fused [q | k | v] row per sequence sets both to (Hq + 2 Hkv) * D.
+    int64_t q_seq_stride, kv_new_seq_stride;
+    // optional float biases added to q, k and v before norm and RoPE ([Hq*D], [Hkv*D], [Hkv*D])
+    const float* q_bias;
+    const float* k_bias;
+    const float* v_bias;
     double inv_freq[kMaxHeadDim / 2];
 };
+__host__ __device__ inline int64_t q_stride_of(const DecodeParams& p) {
+    return p.q_seq_stride ? p.q_seq_stride : (int64_t)p.Hq * p.D;
+}
+__host__ __device__ inline int64_t kvn_stride_of(const DecodeParams& p) {
+    return p.kv_new_seq_stride ? p.kv_new_seq_stride : (int64_t)p.Hkv * p.D;
+}
 
 // Tensor-core split-KV decode for 16-bit caches; returns false when the shape
 // has no tensor-core instantiation (caller then uses the generic kernel).
