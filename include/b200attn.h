@@ -225,6 +225,23 @@ B2A_API int b2a_decode_noalloc(int q_dtype, int cache_dtype, int out_dtype, cons
                                int rope_mode, double rope_theta, int window, const float* q_norm_w,
                                const float* k_norm_w, float norm_eps, void* o, void* stream);
 
+/* Batched Gemma-3 prefill: Gemma3WarpLayer.forwardPrefillBatched (INF/gemma/Gemma3WarpLayer.java:
+ * 395-411) runs QK-norm, RoPE and the KV append per position and then one attention
+ * dispatch per position over [firstValid(p), p]; here all positions take one norm +
+ * rotation pre-pass and one attention launch.  q [B,S,Hq,D], k/v
+ * [B,S,Hkv,D], o [B,S,Hq,D] dense.  q_norm_w / k_norm_w [D] (NULL: no norm) apply the
+ * zero-centred RMSNorm x * rsqrt(mean(x^2) + eps) * (1 + w) with a double sum of
+ * squares (Gemma3ReferenceMath.rmsNormZeroCentered, L25-46) to every q / k head before
+ * the rotation at position pos0 + s (rope_mode GEMMA: applyRopeHalf's double products;
+ * NEOX: float).  window > 0 is the local-layer sliding window (firstValidKey =
+ * max(0, p - window + 1)); scale is 1/sqrt(query_pre_attn_scalar).  k_rot_out (or NULL)
+ * receives the normed, rotated keys in the input type: the rows the KV cache keeps (the
+ * values are appended unchanged). */
+B2A_API int b2a_prefill_gemma(b2a_context* ctx, int in_dtype, int out_dtype, const void* q, const void* k,
+                              const void* v, void* o, int B, int S, int Hq, int Hkv, int D, float scale,
+                              int rope_mode, double rope_theta, int pos0, int window, const float* q_norm_w,
+                              const float* k_norm_w, float norm_eps, void* k_rot_out, void* stream);
+
 /* ------------------------------------------- reference GPU contracts, 1:1 */
 
 /* ROPE_AND_APPEND_HLSL (WB/windows/QwenAttentionShaders.java:82-135), root

@@ -207,3 +207,46 @@ def test_encoder_bf16_inputs(ctx, layout):
     lens = [100, 37, 1, 64]
     got, want = _encoder_case(ctx, B=4, H=3, S=100, D=64, dtype=oracle.BF16, lens=lens, layout=layout, seed=600)
     assert_close(got, want, what="bf16 encoder")
+
+
+@pytest.mark.parametrize("dtype,window,theta,S,D", [
+    (oracle.BF16, 32, 1e4, 96, 256),    # Gemma-3-270M local layer (4/1 heads, D 256)
+    (oracle.BF16, 0, 1e6, 96, 256),     # global layer
+    (oracle.F16, 40, 1e4, 130, 128),    # a tensor-core head dim, ragged last tile
+    (oracle.F32, 0, 1e6, 48, 256),      # fp32 end to end
+])
+def test_prefill_gemma_batched_matches_oracle(ctx, dtype, window, theta, S, D):
+    """b2a_prefill_gemma: QK-norm (zero-centred RMSNorm, (1 + w)) and applyRopeHalf of every
+    position, then one causal attention launch with the local-layer window, against the
+    oracle's restatement of the same steps with the Gemma softmax (double exp-sum)."""
+    import torch
+    import b200attn
+    B, Hq, Hkv, pos0, eps = 2, 4, 1, 3, 1e-6
+    q = normal(41, (B, S, Hq, D), dtype)
+    k = normal(42, (B, S, Hkv, D), dtype)
+    v = normal(43, (B, S, Hkv, D), dtype)
+    qw = (normal(44, (D,), oracle.F32) * 0.5).astype(np.float32)
+    kw = (normal(45, (D,), oracle.F32) * 0.5).astype(np.float32)
+    scale = float(np.float32(1.0 / math.sqrt(256.0)))  # 1/sqrt(query_pre_attn_scalar)
+
+    def norm_rope(x, H, w):
+        out = np.empty_like(x)
+        for b in range(B):
+            for s in range(S):
+                r = oracle.rmsnorm_zero_centered(np.ascontiguousarray(x[b, s]).reshape(-1), H, D, w, eps)
+                out[b, s] = oracle.rope_half_gemma(r, H, D, pos0 + s, theta).reshape(H, D)
+        return out
+
+    q_r, k_r = norm_rope(q, Hq, qw), norm_rope(k, Hkv, kw)
+    want = oracle.prefill(q_r, k_r, v, B=B, S=S, Hq=Hq, Hkv=Hkv, D=D, scale=scale, rope_theta=0.0, window=window,
+                          softmax_mode=oracle.SOFTMAX_GEMMA)
+    o = torch.empty((B, S, Hq, D), dtype=torch.float32, device="cuda")
+    kr = torch.empty((B, S, Hkv, D), dtype=getattr(torch, TORCH[dtype]), device="cuda")
+    b200attn.prefill_gemma(ctx, to_dev(q, dtype), to_dev(k, dtype), to_dev(v, dtype), o, scale,
+                           q_norm_w=torch.from_numpy(qw).cuda(), k_norm_w=torch.from_numpy(kw).cuda(), norm_eps=eps,
+                           rope_mode=b200attn.ROPE_GEMMA, rope_theta=theta, pos0=pos0, window=window, k_rot_out=kr)
+    torch.cuda.synchronize()
+    assert_close(to_np(o), want, atol=1e-4 if dtype == oracle.F32 else 2e-3, what=f"gemma prefill {TORCH[dtype]}")
+    want_k = oracle.round_to(k_r, dtype)
+    ulp = {oracle.F16: 2.0 ** -10, oracle.BF16: 2.0 ** -7, oracle.F32: 2.0 ** -23}[dtype]
+    assert np.all(np.abs(to_np(kr) - want_k) <= ulp * np.maximum(np.abs(want_k), 2.0 ** -14))

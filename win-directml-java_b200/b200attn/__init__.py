@@ -101,11 +101,13 @@ def lib() -> ctypes.CDLL:
         L.b2a_qwen_rope_and_append.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp]
         L.b2a_qwen_gqa_attention_decode.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp]
         L.b2a_qwen_decode_step.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _f, _vp]
+        L.b2a_prefill_gemma.argtypes = [_vp, _i, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _d, _i, _i, _vp,
+                                        _vp, _f, _vp, _vp]
         L.b2a_gemma_fused_attention_context.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp]
         L.b2a_partition_units.argtypes = [_i, _i, _vp, _vp]
         for name in ("b2a_create", "b2a_destroy", "b2a_last_error", "b2a_set_workspace_limit", "b2a_workspace_bytes",
                      "b2a_reserve_decode", "b2a_check_device_status", "b2a_mha", "b2a_prefill_causal", "b2a_decode",
-                     "b2a_qwen_rope_and_append", "b2a_qwen_gqa_attention_decode", "b2a_qwen_decode_step",
+                     "b2a_qwen_rope_and_append", "b2a_qwen_gqa_attention_decode", "b2a_qwen_decode_step", "b2a_prefill_gemma",
                      "b2a_gemma_fused_attention_context", "b2a_partition_units"):
             getattr(L, name).restype = _i
         _lib = L
@@ -241,6 +243,23 @@ def prefill_causal(ctx: Context, q, k, v, o, scale: float, rope_mode: int = ROPE
     ctx.check(lib().b2a_prefill_causal(ctx.handle, _dtype_code(q), _dtype_code(o), _ptr(q), _ptr(k), _ptr(v), _ptr(o),
                                        B, S, Hq, Hkv, D, scale, rope_mode, rope_theta, pos0, window, _ptr(k_rot_out),
                                        _stream(stream)))
+    return o
+
+
+def prefill_gemma(ctx: Context, q, k, v, o, scale: float, *, q_norm_w=None, k_norm_w=None, norm_eps: float = 1e-6,
+                  rope_mode: int = ROPE_GEMMA, rope_theta: float = 10000.0, pos0: int = 0, window: int = 0,
+                  k_rot_out=None, stream=None):
+    """Batched Gemma-3 prefill: QK-norm + RoPE of every position and one causal attention
+    launch (sliding window when window > 0); q [B,S,Hq,D], k/v [B,S,Hkv,D], o [B,S,Hq,D]."""
+    B, S, Hq, D = q.shape
+    Hkv = k.shape[2]
+    if tuple(k.shape) != (B, S, Hkv, D) or tuple(v.shape) != (B, S, Hkv, D):
+        raise ValueError("k and v must be [B,S,Hkv,D] matching q")
+    if tuple(o.shape) != (B, S, Hq, D):
+        raise ValueError("o must be [B,S,Hq,D]")
+    ctx.check(lib().b2a_prefill_gemma(ctx.handle, _dtype_code(q), _dtype_code(o), _ptr(q), _ptr(k), _ptr(v), _ptr(o),
+                                      B, S, Hq, Hkv, D, scale, rope_mode, rope_theta, pos0, window, _ptr(q_norm_w),
+                                      _ptr(k_norm_w), norm_eps, _ptr(k_rot_out), _stream(stream)))
     return o
 
 

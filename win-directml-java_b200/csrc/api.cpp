@@ -502,6 +502,84 @@ B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype, co
     return B2A_OK;
 }
 
+// ----------------------------------------------------------------- Gemma prefill
+B2A_API int b2a_prefill_gemma(b2a_context* ctx, int in_dtype, int out_dtype, const void* q, const void* k, const void* v,
+                              void* o, int B, int S, int Hq, int Hkv, int D, float scale, int rope_mode,
+                              double rope_theta, int pos0, int window, const float* q_norm_w, const float* k_norm_w,
+                              float norm_eps, void* k_rot_out, void* stream) {
+    // Gemma3WarpLayer.forwardPrefillBatched steps 3-4 (INF/gemma/Gemma3WarpLayer.java:395-411): per position QK-norm,
+    // RoPE at p, KV append, then one attention over [firstValid(p), p] per position; here the
+    // norm + rotation of all positions is one pre-pass and the attention one launch.
+    if (!ctx) return B2A_EINVAL;
+    if (!valid_dtype(in_dtype) || !valid_dtype(out_dtype))
+        return fail(ctx, B2A_EINVAL, "unsupported element type (in %d, out %d)", in_dtype, out_dtype);
+    if (!q || !k || !v || !o) return fail(ctx, B2A_EINVAL, "q, k, v and o must not be null");
+    int rc = check_heads(ctx, Hq, Hkv);
+    if (rc) return rc;
+    if ((rc = check_head_dim(ctx, D))) return rc;
+    if (B <= 0 || S <= 0) return fail(ctx, B2A_EINVAL, "batch and sequence length must be > 0");
+    if (window < 0) return fail(ctx, B2A_EINVAL, "window must not be negative");
+    if (pos0 < 0) return fail(ctx, B2A_EINVAL, "pos0 must not be negative");
+    if (rope_mode != B2A_ROPE_NONE && rope_mode != B2A_ROPE_NEOX && rope_mode != B2A_ROPE_GEMMA)
+        return fail(ctx, B2A_EINVAL, "unknown rope mode %d", rope_mode);
+    if (rope_mode != B2A_ROPE_NONE && !(rope_theta > 0.0)) return fail(ctx, B2A_EINVAL, "rope theta must be > 0");
+    if (!(scale == scale) || scale <= 0.f) return fail(ctx, B2A_EINVAL, "scale must be a positive number");
+    if (!(norm_eps >= 0.f)) return fail(ctx, B2A_EINVAL, "norm eps must not be negative");
+    DeviceGuard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+    // same operand rule as b2a_prefill_causal: bf16 inputs are multiplied as fp16
+    const int cdt = in_dtype == B2A_BFLOAT16 ? B2A_FLOAT16 : in_dtype;
+    const size_t ce = dtype_size(cdt);
+    const size_t nq = (size_t)B * S * Hq * D, nk = (size_t)B * S * Hkv * D;
+    auto r256 = [](size_t x) { return (x + 255) / 256 * 256; };
+    const bool rope = rope_mode != B2A_ROPE_NONE;
+    const bool conv = cdt != in_dtype;
+    const size_t table_bytes = rope ? r256((size_t)S * (D / 2) * 16) : 0;
+    const size_t q_bytes = r256(nq * ce), k_bytes = r256(nk * ce), v_bytes = conv ? r256(nk * ce) : 0;
+    rc = ensure_buffer(ctx, &ctx->pf_ws, &ctx->pf_ws_bytes, table_bytes + q_bytes + k_bytes + v_bytes, "prefill");
+    if (rc) return rc;
+    char* base = static_cast<char*>(ctx->pf_ws);
+    double2* table = reinterpret_cast<double2*>(base);
+    void* q_c = base + table_bytes;
+    void* k_c = base + table_bytes + q_bytes;
+    void* v_c = conv ? base + table_bytes + q_bytes + k_bytes : const_cast<void*>(v);
+    double inv[kMaxHeadDim / 2] = {};
+    if (rope) inv_freq_table(rope_theta, D, inv);
+    cudaError_t e = launch_norm_rope_rows(q, q_c, nullptr, in_dtype, cdt, B, S, Hq, D, q_norm_w, norm_eps, rope_mode,
+                                          pos0, inv, table, true, ctx->status, s);
+    if (e == cudaSuccess)
+        e = launch_norm_rope_rows(k, k_c, k_rot_out, in_dtype, cdt, B, S, Hkv, D, k_norm_w, norm_eps, rope_mode, pos0,
+                                  inv, table, false, ctx->status, s);
+    if (e == cudaSuccess && conv) e = launch_convert(v, in_dtype, v_c, cdt, (int64_t)nk, ctx->status, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "norm / rope / conversion kernel launch");
+
+    AttnParams p{};
+    p.q = q_c;
+    p.k = k_c;
+    p.v = v_c;
+    p.in_dtype = cdt;
+    p.o = o;
+    p.out_dtype = out_dtype;
+    p.B = B;
+    p.S = S;
+    p.Hq = Hq;
+    p.Hkv = Hkv;
+    p.D = D;
+    p.q_sb = (int64_t)S * Hq * D;
+    p.q_ss = (int64_t)Hq * D;
+    p.q_sh = D;
+    p.k_sb = (int64_t)S * Hkv * D;
+    p.k_ss = (int64_t)Hkv * D;
+    p.k_sh = D;
+    p.causal = 1;
+    p.window = window;
+    p.scale = scale;
+    e = launch_attention(ctx, p, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "attention kernel launch");
+    return B2A_OK;
+}
+
 // ----------------------------------------------------------------- decode
 B2A_API int b2a_decode(b2a_context* ctx, int q_dtype, int cache_dtype, int out_dtype, const void* q_new,
                        const void* k_new, const void* v_new, void* k_cache, void* v_cache, int kv_layout,

@@ -125,6 +125,15 @@ bool prep_vectorizable(int D, int64_t elems, const void* const* ptrs, int n);
 cudaError_t launch_prep(const PrepJob* jobs, int n_jobs, int B, int S, int D, int in_dtype, int out_dtype, int pos0,
                         int rope_mode, const double* inv_freq, double2* table, int* status, cudaStream_t stream);
 
+// QK-norm + RoPE pre-pass (one warp per [b][s][h] row of a dense tensor): zero-centred
+// RMSNorm with (1 + w) when norm_w is set, rotation at pos0 + s (rope_mode 1 NeoX,
+// 2 Gemma) from a double (cos, sin) table built here when build_table is set; writes
+// dst in out_dtype and, when dst_in is set, the same rows in in_dtype.
+cudaError_t launch_norm_rope_rows(const void* src, void* dst, void* dst_in, int in_dtype, int out_dtype, int B, int S,
+                                  int H, int D, const float* norm_w, float eps, int rope_mode, int pos0,
+                                  const double* inv_freq, double2* table, bool build_table, int* status,
+                                  cudaStream_t stream);
+
 // Sets the message b2a_last_error(NULL, ...) returns on this thread.
 void set_thread_error(const char* msg);
 

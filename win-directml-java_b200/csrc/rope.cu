@@ -277,6 +277,70 @@ __global__ void __launch_bounds__(256, 2) prep_kernel(const __grid_constant__ Pr
     }
 }
 
+// ---------------------------------------------------------------- QK-norm + RoPE rows
+__device__ __forceinline__ double warp_sum_double(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// One warp per [b][s][h] row: zero-centred RMSNorm with (1 + w)
+// (Gemma3ReferenceMath.rmsNormZeroCentered, INF/gemma/Gemma3ReferenceMath.java:25-46:
+// double sum of squares, float rms, (float)(x * rms * (1 + w))), then the rotation at
+// position pos0 + s from the double table (Gemma: double products; NeoX: float), into
+// dst (out_dtype) and, when set, dst_in (the input dtype: the rows the KV cache keeps).
+__global__ void __launch_bounds__(256) norm_rope_rows_kernel(const void* src, void* dst, void* dst_in, int in_dtype,
+                                                            int out_dtype, int64_t rows, int S, int H, int D,
+                                                            const float* norm_w, float eps, int rope_mode,
+                                                            const double2* table, int* status) {
+    extern __shared__ float nr_sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* vec = nr_sm + warp * D;
+    const int half = D / 2;
+    for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < rows; row += (int64_t)gridDim.x * 8) {
+        const int s = (int)((row / H) % S);
+        const int64_t off = row * D;
+        double ss = 0.0;
+        for (int d = lane; d < D; d += 32) {
+            const float x = load_as_float(src, off + d, in_dtype);
+            vec[d] = x;
+            ss += (double)x * (double)x;
+        }
+        __syncwarp();
+        if (norm_w != nullptr) {
+            ss = warp_sum_double(ss);
+            const float rms = (float)(1.0 / sqrt(__dadd_rn(ss / (double)D, (double)eps)));
+            for (int d = lane; d < D; d += 32)
+                vec[d] = (float)__dmul_rn((double)__fmul_rn(vec[d], rms), __dadd_rn(1.0, (double)norm_w[d]));
+            __syncwarp();
+        }
+        if (rope_mode != 0) {
+            for (int i = lane; i < half; i += 32) {
+                const double2 t = table[(int64_t)s * half + i];
+                const float a = vec[i], b = vec[i + half];
+                float y0, y1;
+                if (rope_mode == 2) {
+                    y0 = (float)__dsub_rn(__dmul_rn((double)a, t.x), __dmul_rn((double)b, t.y));
+                    y1 = (float)__dadd_rn(__dmul_rn((double)b, t.x), __dmul_rn((double)a, t.y));
+                } else {
+                    const float cf = (float)t.x, sf = (float)t.y;
+                    y0 = __fsub_rn(__fmul_rn(a, cf), __fmul_rn(b, sf));
+                    y1 = __fadd_rn(__fmul_rn(a, sf), __fmul_rn(b, cf));
+                }
+                vec[i] = y0;  // each pair belongs to one lane
+                vec[i + half] = y1;
+            }
+            __syncwarp();
+        }
+        for (int d = lane; d < D; d += 32) {
+            store_from_float(dst, off + d, vec[d], out_dtype);
+            flag_overflow(vec[d], round_through(vec[d], out_dtype), status);
+            if (dst_in != nullptr) store_from_float(dst_in, off + d, vec[d], in_dtype);
+        }
+        __syncwarp();
+    }
+}
+
 }  // namespace
 
 // `table` is a device buffer of S * D/2 double2 entries owned by the caller;
@@ -371,6 +435,28 @@ cudaError_t launch_prep(const PrepJob* jobs, int n_jobs, int B, int S, int D, in
         if (gemma) prep_kernel<2, true, 1><<<grid, 256, 0, stream>>>(p);
         else prep_kernel<1, true, 2><<<grid, 256, 0, stream>>>(p);
     }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_norm_rope_rows(const void* src, void* dst, void* dst_in, int in_dtype, int out_dtype, int B, int S,
+                                  int H, int D, const float* norm_w, float eps, int rope_mode, int pos0,
+                                  const double* inv_freq, double2* table, bool build_table, int* status,
+                                  cudaStream_t stream) {
+    const int half = D / 2;
+    if (rope_mode != 0 && build_table) {
+        FreqTable f{};
+        for (int i = 0; i < half; ++i) f.inv_freq[i] = inv_freq[i];
+        const int64_t n = (int64_t)S * half;
+        const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+        rope_table_kernel<<<grid, 256, 0, stream>>>(table, S, half, pos0, f);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    const int64_t rows = (int64_t)B * S * H;
+    const int64_t blocks = (rows + 7) / 8;
+    const int grid = (int)(blocks < 148 * 16 ? blocks : 148 * 16);
+    norm_rope_rows_kernel<<<grid, 256, (size_t)8 * D * sizeof(float), stream>>>(
+        src, dst, dst_in, in_dtype, out_dtype, rows, S, H, D, norm_w, eps, rope_mode, table, status);
     return cudaGetLastError();
 }
 
