@@ -6,13 +6,17 @@
 // in three warpgroups:
 //   warps 0-3  softmax of tile A, warps 4-7 softmax of tile B: thread t of a
 //              group owns query row t = TMEM lane t (tcgen05.ld/st 32x32b);
-//   warp 8     TMA producer: Q_A, Q_B once, then K and V tiles of 128 keys
-//              into a 2-3 stage ring (plain tiled loads, 128-byte swizzle,
-//              64-element panels of the head dimension);
+//   warp 8     TMA producer: Q_A, Q_B once, then ring items of two 128-key
+//              tiles, K(i) and V(i-1), into a 2-3 stage ring (plain tiled
+//              loads, 128-byte swizzle, 64-element panels of the head dim);
 //   warp 9     MMA issuer (the whole warp runs the loop, lane 0 issues).  Per
 //              key tile j: O_A += P_A(j) V_j, S_A = Q_A K_{j+1}^T, then the same
 //              for B, so the tensor core works on one tile while the softmax
-//              group of the other runs (ping-pong);
+//              group of the other runs (ping-pong).  Its per-step overhead
+//              (barrier waits, commits) sits between MMA runs with the tensor
+//              core idle -- issue blocks while earlier MMAs execute -- so it
+//              waits once per step for the ring item and commits O only after
+//              a tile's last PV;
 //   warps 10-11 idle.
 // setmaxnreg moves registers from the control warpgroup (8-11) to the softmax
 // warpgroups, which keep a whole score row (128 fp32) in registers.
@@ -346,16 +350,16 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const uint32_t bar0 = base + Gm::oBar;
     // barriers, 8 bytes each
     const uint32_t bQ = bar0;
-    // K and V have separate rings: K(j) is last read by QK(j) one step before V(j) is
-    // last read by PV(j), so its stage is refilled that much earlier
-    auto bKfull = [&](int s) { return bar0 + 8u * (1 + s); };
-    auto bKempty = [&](int s) { return bar0 + 8u * (1 + ST + s); };
-    auto bVfull = [&](int s) { return bar0 + 8u * (1 + 2 * ST + s); };
-    auto bVempty = [&](int s) { return bar0 + 8u * (1 + 3 * ST + s); };
-    auto bSfull = [&](int t) { return bar0 + 8u * (1 + 4 * ST + t); };
-    auto bPfull = [&](int t) { return bar0 + 8u * (3 + 4 * ST + t); };
-    auto bOdone = [&](int t) { return bar0 + 8u * (5 + 4 * ST + t); };
-    const uint32_t bDrain = bar0 + 8u * (7 + 4 * ST);
+    // Ring item i holds K(i) (i < n_max) and V(i-1) (i >= 1): step j reads V(j) and then
+    // K(j+1), both last in the same step, so one stage, one full and one empty barrier
+    // serve the pair (one wait and one release per step on the MMA thread).  K(i) sits
+    // in stage i % ST of the K ring, V(i-1) in stage i % ST of the V ring.
+    auto bKVfull = [&](int s) { return bar0 + 8u * (1 + s); };
+    auto bKVempty = [&](int s) { return bar0 + 8u * (1 + ST + s); };
+    auto bSfull = [&](int t) { return bar0 + 8u * (1 + 2 * ST + t); };
+    auto bPfull = [&](int t) { return bar0 + 8u * (3 + 2 * ST + t); };
+    auto bOdone = [&](int t) { return bar0 + 8u * (5 + 2 * ST + t); };
+    const uint32_t bDrain = bar0 + 8u * (7 + 2 * ST);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(base_ptr + Gm::oBar + 256);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(base_ptr + Gm::oBar + 264);
 
@@ -391,15 +395,16 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     }
     const int t_begin = kb[0] / kBN;  // tile A starts no later than tile B
     for (int t = 0; t < 2; ++t) nt[t] = q0t[t] < S ? (ke[t] + kBN - 1) / kBN - t_begin : 0;
-    const int n_max = max(nt[0], nt[1]);
+    // scalars: the roles' loops select between them instead of indexing the arrays with
+    // a runtime tile index (which would put the arrays in local memory)
+    const int nt0 = nt[0], nt1 = nt[1];
+    const int n_max = max(nt0, nt1);
 
     if (tid == 0) {
         mbar_init(bQ, 1);
         for (int s = 0; s < ST; ++s) {
-            mbar_init(bKfull(s), 1);
-            mbar_init(bKempty(s), 1);
-            mbar_init(bVfull(s), 1);
-            mbar_init(bVempty(s), 1);
+            mbar_init(bKVfull(s), 1);
+            mbar_init(bKVempty(s), 1);
         }
         for (int t = 0; t < 2; ++t) {
             mbar_init(bSfull(t), 1);
@@ -426,36 +431,31 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       if (warp == 8) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            int k_issued = 0, v_issued = 0;
-            // one K or V tile into its ring stage, after the stage's previous tile was released
-            auto load = [&](const CUtensorMap* map, uint32_t ring, int j, bool is_k) -> bool {
-                const int st = j % ST;
-                const uint32_t full = is_k ? bKfull(st) : bVfull(st), empty = is_k ? bKempty(st) : bVempty(st);
-                if (j >= ST && !mbar_wait(empty, ((j / ST) - 1) & 1, abort_flag, status)) return false;
-                mbar_expect_tx(full, Gm::kTxTile);
-                for (int pn = 0; pn < NP; ++pn)
-                    tma_load_4d(ring + st * Gm::kTileBytes + pn * Gm::kPanelBytes, map, full, 64 * pn, kvh,
-                                (t_begin + j) * kBN, b);
-                return true;
-            };
             mbar_expect_tx(bQ, 2 * Gm::kTileBytes);
             for (int t = 0; t < 2; ++t)
                 for (int pn = 0; pn < NP; ++pn)
                     tma_load_4d(sQ + t * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmQ, bQ, 64 * pn, h, q0t[t], b);
-            // K runs one tile ahead of V: K(0), then K(i+1), V(i)
-            if (n_max > 0 && load(&tmK, sK, 0, true)) k_issued = 1;
-            for (int i = 0; i < n_max && k_issued > i; ++i) {
-                if (i + 1 < n_max) {
-                    if (!load(&tmK, sK, i + 1, true)) break;
-                    k_issued = i + 2;
-                }
-                if (!load(&tmV, sV, i, false)) break;
-                v_issued = i + 1;
+            // ring items 0..n_max: K(i) and V(i-1), each into its stage after the stage's
+            // previous item was released
+            int issued = 0;
+            for (int i = 0; n_max > 0 && i <= n_max; ++i) {
+                const int st = i % ST;
+                if (i >= ST && !mbar_wait(bKVempty(st), ((i / ST) - 1) & 1, abort_flag, status)) break;
+                const bool has_k = i < n_max, has_v = i >= 1;
+                mbar_expect_tx(bKVfull(st), (has_k ? Gm::kTxTile : 0u) + (has_v ? Gm::kTxTile : 0u));
+                if (has_k)
+                    for (int pn = 0; pn < NP; ++pn)
+                        tma_load_4d(sK + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmK, bKVfull(st), 64 * pn, kvh,
+                                    (t_begin + i) * kBN, b);
+                if (has_v)
+                    for (int pn = 0; pn < NP; ++pn)
+                        tma_load_4d(sV + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmV, bKVfull(st), 64 * pn, kvh,
+                                    (t_begin + i - 1) * kBN, b);
+                issued = i + 1;
             }
             // every copy this thread issued lands before the CTA may exit
             mbar_drain(bQ, 0);
-            for (int j = (k_issued > ST ? k_issued - ST : 0); j < k_issued; ++j) mbar_drain(bKfull(j % ST), (j / ST) & 1);
-            for (int j = (v_issued > ST ? v_issued - ST : 0); j < v_issued; ++j) mbar_drain(bVfull(j % ST), (j / ST) & 1);
+            for (int i = (issued > ST ? issued - ST : 0); i < issued; ++i) mbar_drain(bKVfull(i % ST), (i / ST) & 1);
         }
     } else if (warp == 9) {
         // ------------------------------------------------------------ MMA issuer
@@ -465,26 +465,16 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             const uint32_t ln = (uint32_t)lane;
             const uint32_t idq = make_idesc(p.fmt, kBM, kBN, 0, 0);
             const uint32_t idp = make_idesc(p.fmt, kBM, D, 0, 1);
-            int k_ready = -1, v_ready = -1;  // highest key tile whose K / V wait was observed
+            int item_ready = -1;  // highest ring item whose full wait was observed
             bool ok = __all_sync(0xffffffffu, mbar_wait(bQ, 0, abort_flag, status));
-            auto wait_k = [&](int j) -> bool {
-                if (k_ready >= j) return true;
-                if (!__all_sync(0xffffffffu, mbar_wait(bKfull(j % ST), (j / ST) & 1, abort_flag, status)))
+            auto wait_item = [&](int i) -> bool {
+                if (item_ready >= i) return true;
+                if (!__all_sync(0xffffffffu, mbar_wait(bKVfull(i % ST), (i / ST) & 1, abort_flag, status)))
                     return false;
                 tc_fence_after();
-                k_ready = j;
+                item_ready = i;
                 return true;
             };
-            auto wait_v = [&](int j) -> bool {
-                if (v_ready >= j) return true;
-                if (!__all_sync(0xffffffffu, mbar_wait(bVfull(j % ST), (j / ST) & 1, abort_flag, status)))
-                    return false;
-                tc_fence_after();
-                v_ready = j;
-                return true;
-            };
-            // the tile that reads K(j) / V(j) last (tile B unless it has no key tile j)
-            auto last_tile = [&](int j) { return j < nt[1] ? 1 : 0; };
             // descriptors of each buffer's start: a K step, tile or stage offset only moves the
             // 14-bit start-address field (addr >> 4) of the low word, and every offset here stays inside it
             const uint64_t dQ = smem_desc(sQ, 16, 1024), dK = smem_desc(sK, 16, 1024);
@@ -504,45 +494,45 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 umma_commit_w(ln, bSfull(t));
             };
             auto issue_pv = [&](int t, int j) {
-                // V tile, MN-major: 8-key atoms 1024 B apart (SBO), 64-column panels kPanelBytes apart (LBO)
-                const uint32_t b0 = v_lo + (uint32_t)((j % ST) * Gm::kTileBytes >> 4);
+                // V(j) (ring item j+1), MN-major: 8-key atoms 1024 B apart (SBO), 64-column panels kPanelBytes
+                // apart (LBO)
+                const uint32_t b0 = v_lo + (uint32_t)(((j + 1) % ST) * Gm::kTileBytes >> 4);
                 const uint32_t d = tmem + 256u + 128u * t, a = tmem + 128u * t;
                 umma_ts_w<-1>(ln, d, a, b0, v_hi, idp, j > 0 ? 1u : 0u);
 #pragma unroll
                 for (int kk = 1; kk < kBN / 16; ++kk) umma_ts_w<1>(ln, d, a + kk * 8u, b0 + kk * 128u, v_hi, idp);
-                umma_commit_w(ln, bOdone(t));
             };
             if (ok && n_max > 0) {
-                ok = wait_k(0);
-                for (int t = 0; t < 2 && ok; ++t)
-                    if (nt[t] > 0) issue_qk(t, 0);
-                if (ok) umma_commit_w(ln, bKempty(0));
+                ok = wait_item(0);
+                if (ok && nt0 > 0) issue_qk(0, 0);
+                if (ok && nt1 > 0) issue_qk(1, 0);
+                if (ok) umma_commit_w(ln, bKVempty(0));  // item 0 (K(0)) read by both tiles
             }
             for (int j = 0; j < n_max && ok; ++j) {
+                // the tile whose part of this step reads item j+1 last: tile B whenever it takes
+                // part (its rows follow tile A's, so nt0 <= nt1 unless tile B is empty)
+                const int rel = j < nt1 ? 1 : 0;
                 // rolled over the two tiles: unrolled, each tile's per-step descriptor words
                 // would be loop-invariant and hoisted into (spilled) registers
 #pragma unroll 1
                 for (int t = 0; t < 2 && ok; ++t) {
-                    if (j >= nt[t]) continue;
+                    const int ntt = t ? nt1 : nt0;
+                    if (j >= ntt) continue;
                     if (!__all_sync(0xffffffffu, mbar_wait(bPfull(t), j & 1, abort_flag, status))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    if (!wait_v(j)) {
+                    if (!wait_item(j + 1)) {  // V(j), K(j+1)
                         ok = false;
                         break;
                     }
                     issue_pv(t, j);
-                    if (t == last_tile(j)) umma_commit_w(ln, bVempty(j % ST));  // V(j) read for the last time
-                    if (j + 1 < nt[t]) {
-                        if (!wait_k(j + 1)) {
-                            ok = false;
-                            break;
-                        }
-                        issue_qk(t, j + 1);
-                        if (t == last_tile(j + 1)) umma_commit_w(ln, bKempty((j + 1) % ST));
-                    }
+                    // O_t is complete after its last PV; earlier PVs need no signal of their own:
+                    // S_t(j+1) is committed after PV_t(j), and a commit tracks every earlier MMA
+                    if (j + 1 == ntt) umma_commit_w(ln, bOdone(t));
+                    if (j + 1 < ntt) issue_qk(t, j + 1);
+                    if (t == rel) umma_commit_w(ln, bKVempty((j + 1) % ST));
                 }
             }
             // all MMAs lane 0 issued are complete before TMEM is released
@@ -624,12 +614,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 const float m_new = need ? mx : m_run;
                 const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
                 l_run *= alpha;
+                // O_t holds PV(j-1) complete: S_t(j), waited for above, was committed after it
                 if (j > 0) {
-                    if (!__all_sync(0xffffffffu, mbar_wait(bOdone(t), (j - 1) & 1, abort_flag, status))) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
 #pragma unroll
                     for (int c = 0; c < D / 32; ++c) {
                         uint32_t o[32];
@@ -673,7 +659,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             mbar_arrive(bPfull(t));
         }
         // epilogue: O / l for rows inside the sequence
-        if (ok && my_nt > 0 && __all_sync(0xffffffffu, mbar_wait(bOdone(t), (my_nt - 1) & 1, abort_flag, status))) {
+        if (ok && my_nt > 0 && __all_sync(0xffffffffu, mbar_wait(bOdone(t), 0, abort_flag, status))) {
             tc_fence_after();
             const float inv = 1.f / l_run;
 #pragma unroll
