@@ -23,7 +23,7 @@ struct b2a_context {
     int sm_count = 0;
     std::string last_error;
     size_t ws_limit = 0;  // 0: unlimited
-    int* status = nullptr;  // device int[4]
+    int* status = nullptr;  // device int[kStatusBufferInts]: error flags, prefill work-item counters
     // decode workspace: [counters][partials]
     void* dec_ws = nullptr;
     size_t dec_ws_bytes = 0;
@@ -223,8 +223,8 @@ B2A_API int b2a_create(int device, b2a_context** out) {
     if (!ctx) return fail(nullptr, B2A_EOOM, "host allocation failed");
     ctx->device = device;
     ctx->sm_count = prop.multiProcessorCount;
-    e = cudaMalloc(&ctx->status, 4 * sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(ctx->status, 0, 4 * sizeof(int));
+    e = cudaMalloc(&ctx->status, kStatusBufferInts * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ctx->status, 0, kStatusBufferInts * sizeof(int));
     if (e != cudaSuccess) {
         delete ctx;
         return fail(nullptr, B2A_ECUDA, "status buffer: %s", cudaGetErrorString(e));
@@ -299,7 +299,7 @@ B2A_API int b2a_check_device_status(b2a_context* ctx, void* stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "stream synchronize");
-    int st[4] = {0, 0, 0, 0};
+    int st[kStatusWords] = {0, 0, 0, 0};
     e = cudaMemcpy(st, ctx->status, sizeof(st), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "status read");
     if (st[0] == 0) return B2A_OK;

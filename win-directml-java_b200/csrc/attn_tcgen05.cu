@@ -44,6 +44,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -61,8 +62,8 @@ constexpr int kThreadsTc = 384;
 // the two softmax warpgroups can keep a whole 128-column score row resident.
 // 2 * kRegsSoftmax + kRegsControl == 3 * kRegsLaunch: the pool is used exactly.
 constexpr int kRegsLaunch = 168;
-constexpr int kRegsSoftmax = 224;
-constexpr int kRegsControl = 56;
+constexpr int kRegsSoftmax = 216;
+constexpr int kRegsControl = 72;
 static_assert(2 * kRegsSoftmax + kRegsControl == 3 * kRegsLaunch, "register split must equal the launch pool");
 constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s
 constexpr float kRescaleThreshold = 8.0f;
@@ -84,6 +85,8 @@ struct TcParams {
     int64_t o_sb, o_ss, o_sh;
     int* status;
     int fmt;  // 0 = fp16, 1 = bf16 operands
+    int* sched;   // device int[2]: next work item, CTAs finished (zero between launches)
+    int n_items;  // work items: query-tile pairs x heads x batch
 };
 
 template <int D>
@@ -96,7 +99,7 @@ struct TcGeo {
     static constexpr int oK = 2 * kTileBytes;
     static constexpr int oV = oK + kStages * kTileBytes;
     static constexpr int oBar = oV + kStages * kTileBytes;
-    static constexpr int kBytes = oBar + 512;
+    static constexpr int kBytes = oBar + 512;  // barriers, TMEM address, abort flag, work-item mailbox
     static constexpr uint32_t kTxTile = kTileBytes;  // bytes one K or V tile load delivers (zero fill included)
     static_assert(kBytes + 1024 <= 227 * 1024, "shared memory budget");
 };
@@ -336,6 +339,98 @@ __device__ __forceinline__ void store8(void* out, int64_t off, const float* v, i
 // ---------------------------------------------------------------- kernel
 // kAdditive: the additive [B][S] key mask is applied (its own instantiation, so the
 // mask loads do not weigh on the register budget of the unmasked kernels).
+// A work item is the pair of query tiles (A, B) starting at row 2 * 128 * pair of one
+// (batch, head).  Items are numbered pair-fastest, longest causal pair first within a
+// head: w = x + n_pairs * (h + Hq * b), pair = n_pairs - 1 - x when causal.  CTAs take
+// items in that order from a device counter, so the heads in flight at any time are a
+// few consecutive ones (their K/V stay in L2) and the longest items start first.
+struct ItemGeo {
+    int b, h;
+    int q0a, q0b;     // first query row of tile A / B
+    int kb0, kb1;     // first visible key of tile A / B (sliding window)
+    int ke0, ke1;     // key end of tile A / B
+    int t_begin;      // first key tile (tile A's window start)
+    int nt0, nt1;     // key tiles of tile A / B from t_begin (0: tile beyond S)
+    int n_max;
+    bool uniform;     // no valid key (key_len <= 0): every key weighs the same
+};
+
+__device__ __forceinline__ ItemGeo item_geo(int w, int n_pairs, int Hq, int S, int causal, int window,
+                                            const int32_t* key_len) {
+    ItemGeo g;
+    const int x = w % n_pairs, rest = w / n_pairs;
+    g.h = rest % Hq;
+    g.b = rest / Hq;
+    const int pair = causal ? n_pairs - 1 - x : x;
+    g.q0a = pair * 2 * kBM;
+    g.q0b = g.q0a + kBM;
+    g.kb0 = g.kb1 = 0;
+    g.ke0 = g.ke1 = S;
+    g.uniform = false;
+    if (causal) {
+        g.ke0 = min(S, g.q0a + kBM);
+        g.ke1 = min(S, g.q0b + kBM);
+        if (window > 0) {
+            g.kb0 = max(0, g.q0a - window + 1);
+            g.kb1 = max(0, g.q0b - window + 1);
+        }
+    } else if (key_len != nullptr) {
+        const int kl = key_len[g.b];
+        if (kl <= 0) g.uniform = true;
+        else g.ke0 = g.ke1 = min(kl, S);
+    }
+    g.t_begin = g.kb0 / kBN;  // tile A starts no later than tile B
+    g.nt0 = (g.ke0 + kBN - 1) / kBN - g.t_begin;  // q0a < S for every item
+    g.nt1 = g.q0b < S ? (g.ke1 + kBN - 1) / kBN - g.t_begin : 0;
+    g.n_max = max(g.nt0, g.nt1);
+    return g;
+}
+
+// Work-item mailbox slot (ints): the producer computes an item's geometry once and
+// publishes it; the MMA warp and the softmax groups read the fields they use from shared
+// memory, so no role keeps the geometry's inputs or the whole geometry in registers.
+constexpr int kSlotValid = 0;  // 0: no more items
+constexpr int kSlotB = 1, kSlotH = 2, kSlotQ0a = 3, kSlotQ0b = 4;
+constexpr int kSlotKb0 = 5, kSlotKb1 = 6, kSlotKe0 = 7, kSlotKe1 = 8;
+constexpr int kSlotTBegin = 9, kSlotNt0 = 10, kSlotNt1 = 11, kSlotUniform = 12;
+// key tiles starting in [kSlotIntLo_t, kSlotIntHi_t] are interior for every row of tile t
+constexpr int kSlotIntLo0 = 13, kSlotIntHi0 = 14, kSlotIntLo1 = 15, kSlotIntHi1 = 16;
+constexpr int kSlotInts = 24;
+
+__device__ __forceinline__ void publish_item(volatile int* ms, bool valid, const ItemGeo& g, int causal, int window) {
+    ms[kSlotValid] = valid ? 1 : 0;
+    if (!valid) return;
+    ms[kSlotB] = g.b;
+    ms[kSlotH] = g.h;
+    ms[kSlotQ0a] = g.q0a;
+    ms[kSlotQ0b] = g.q0b;
+    ms[kSlotKb0] = g.kb0;
+    ms[kSlotKb1] = g.kb1;
+    ms[kSlotKe0] = g.ke0;
+    ms[kSlotKe1] = g.ke1;
+    ms[kSlotTBegin] = g.t_begin;
+    ms[kSlotNt0] = g.nt0;
+    ms[kSlotNt1] = g.nt1;
+    ms[kSlotUniform] = g.uniform ? 1 : 0;
+    // a key tile [n0, n0 + 128) needs no per-element mask when it lies inside the key range,
+    // wholly at or below the diagonal of the tile's first row and wholly inside the window of
+    // its last row
+    for (int t = 0; t < 2; ++t) {
+        const int q_first = t ? g.q0b : g.q0a, q_last = q_first + kBM - 1;
+        int lo = t ? g.kb1 : g.kb0, hi = (t ? g.ke1 : g.ke0) - kBN;
+        if (causal) {
+            hi = min(hi, q_first - kBN + 1);
+            if (window > 0) lo = max(lo, q_last - window + 1);
+        }
+        if (g.uniform) {
+            lo = 1;
+            hi = 0;
+        }
+        ms[t ? kSlotIntLo1 : kSlotIntLo0] = lo;
+        ms[t ? kSlotIntHi1 : kSlotIntHi0] = hi;
+    }
+}
+
 template <int D, bool kAdditive>
 __global__ void __launch_bounds__(kThreadsTc, 1)
     attn_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -348,68 +443,50 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     unsigned char* base_ptr = smem_raw + (base - smem_u32(smem_raw));
     const uint32_t sQ = base + Gm::oQ, sK = base + Gm::oK, sV = base + Gm::oV;
     const uint32_t bar0 = base + Gm::oBar;
-    // barriers, 8 bytes each
-    const uint32_t bQ = bar0;
-    // Ring item i holds K(i) (i < n_max) and V(i-1) (i >= 1): step j reads V(j) and then
-    // K(j+1), both last in the same step, so one stage, one full and one empty barrier
-    // serve the pair (one wait and one release per step on the MMA thread).  K(i) sits
-    // in stage i % ST of the K ring, V(i-1) in stage i % ST of the V ring.
-    auto bKVfull = [&](int s) { return bar0 + 8u * (1 + s); };
-    auto bKVempty = [&](int s) { return bar0 + 8u * (1 + ST + s); };
-    auto bSfull = [&](int t) { return bar0 + 8u * (1 + 2 * ST + t); };
-    auto bPfull = [&](int t) { return bar0 + 8u * (3 + 2 * ST + t); };
-    auto bOdone = [&](int t) { return bar0 + 8u * (5 + 2 * ST + t); };
-    const uint32_t bDrain = bar0 + 8u * (7 + 2 * ST);
+    // barriers, 8 bytes each.  Every phase count runs on across the CTA's work items.
+    // Q_t: loaded per item, released by the commit after the item's last QK of tile t
+    auto bQfull = [&](int t) { return bar0 + 8u * (0 + t); };
+    auto bQempty = [&](int t) { return bar0 + 8u * (2 + t); };
+    // Ring item i of a work item holds K(i) (i < n_max) and V(i-1) (i >= 1): step j reads
+    // V(j) and then K(j+1), both last in the same step, so one stage, one full and one
+    // empty barrier serve the pair (one wait and one release per step on the MMA thread).
+    // The ring's item count g runs across work items: K and V of ring item g sit in stage
+    // g % ST of the K and V rings.
+    auto bKVfull = [&](int s) { return bar0 + 8u * (4 + s); };
+    auto bKVempty = [&](int s) { return bar0 + 8u * (4 + ST + s); };
+    auto bSfull = [&](int t) { return bar0 + 8u * (4 + 2 * ST + t); };
+    auto bPfull = [&](int t) { return bar0 + 8u * (6 + 2 * ST + t); };
+    auto bOdone = [&](int t) { return bar0 + 8u * (8 + 2 * ST + t); };
+    // work-item mailbox: the producer publishes item k in slot k % 2; the MMA warp and the
+    // eight softmax warps each release it once read
+    auto bItemFull = [&](int s) { return bar0 + 8u * (10 + 2 * ST + s); };
+    auto bItemEmpty = [&](int s) { return bar0 + 8u * (12 + 2 * ST + s); };
+    const uint32_t bDrain = bar0 + 8u * (14 + 2 * ST);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(base_ptr + Gm::oBar + 256);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(base_ptr + Gm::oBar + 264);
+    // mailbox slot s: kSlotInts ints at oBar + 288 + 4 kSlotInts s, a work item's geometry
+    volatile int* slots = reinterpret_cast<volatile int*>(base_ptr + Gm::oBar + 288);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // parameter fields copied to registers once: the asm statements below clobber
     // memory, which would otherwise force a reload through a generic pointer at
     // every use (a 25x slower masked softmax tile when the mask test read them)
-    const int S = p.S, causal = p.causal, window = p.window;
-    const float* const mask = kAdditive ? p.mask : nullptr;
-    const float scale = p.scale;
+    const int n_items = p.n_items;
     int* const status = p.status;
-    const int n_pairs = (S + 2 * kBM - 1) / (2 * kBM);
-    const int pair = causal ? n_pairs - 1 - (int)blockIdx.x : (int)blockIdx.x;
-    const int h = blockIdx.y, b = blockIdx.z;
-    const int kvh = h / p.G;
-    const int qbase = pair * 2 * kBM;
-
-    // per query tile: first row, key range, number of key tiles
-    int q0t[2], kb[2], ke[2], nt[2];
-    bool uniform = false;
-    for (int t = 0; t < 2; ++t) {
-        q0t[t] = qbase + t * kBM;
-        kb[t] = 0;
-        ke[t] = S;
-        if (causal) {
-            ke[t] = min(S, q0t[t] + kBM);
-            if (window > 0) kb[t] = max(0, q0t[t] - window + 1);
-        } else if (p.key_len != nullptr) {
-            const int kl = p.key_len[b];
-            if (kl <= 0) uniform = true;
-            else ke[t] = min(kl, S);
-        }
-    }
-    const int t_begin = kb[0] / kBN;  // tile A starts no later than tile B
-    for (int t = 0; t < 2; ++t) nt[t] = q0t[t] < S ? (ke[t] + kBN - 1) / kBN - t_begin : 0;
-    // scalars: the roles' loops select between them instead of indexing the arrays with
-    // a runtime tile index (which would put the arrays in local memory)
-    const int nt0 = nt[0], nt1 = nt[1];
-    const int n_max = max(nt0, nt1);
 
     if (tid == 0) {
-        mbar_init(bQ, 1);
-        for (int s = 0; s < ST; ++s) {
-            mbar_init(bKVfull(s), 1);
-            mbar_init(bKVempty(s), 1);
-        }
         for (int t = 0; t < 2; ++t) {
+            mbar_init(bQfull(t), 1);
+            mbar_init(bQempty(t), 1);
             mbar_init(bSfull(t), 1);
             mbar_init(bPfull(t), 128);
             mbar_init(bOdone(t), 1);
+            mbar_init(bItemFull(t), 1);
+            mbar_init(bItemEmpty(t), 9);
+        }
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(bKVfull(s), 1);
+            mbar_init(bKVempty(s), 1);
         }
         mbar_init(bDrain, 1);
         *abort_flag = 0;
@@ -431,31 +508,62 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       if (warp == 8) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            mbar_expect_tx(bQ, 2 * Gm::kTileBytes);
-            for (int t = 0; t < 2; ++t)
-                for (int pn = 0; pn < NP; ++pn)
-                    tma_load_4d(sQ + t * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmQ, bQ, 64 * pn, h, q0t[t], b);
-            // ring items 0..n_max: K(i) and V(i-1), each into its stage after the stage's
-            // previous item was released
-            int issued = 0;
-            for (int i = 0; n_max > 0 && i <= n_max; ++i) {
-                const int st = i % ST;
-                if (i >= ST && !mbar_wait(bKVempty(st), ((i / ST) - 1) & 1, abort_flag, status)) break;
-                const bool has_k = i < n_max, has_v = i >= 1;
-                mbar_expect_tx(bKVfull(st), (has_k ? Gm::kTxTile : 0u) + (has_v ? Gm::kTxTile : 0u));
-                if (has_k)
+            const int S = p.S, causal = p.causal, window = p.window, Hq = p.Hq, G = p.G;
+            const int32_t* const key_len = p.key_len;
+            int* const sched = p.sched;
+            const int n_pairs = (S + 2 * kBM - 1) / (2 * kBM);
+            int k = 0;        // work items published
+            int g = 0;        // ring items issued
+            int q_items = 0;  // work items whose Q tiles were issued
+            for (;; ++k) {
+                const int slot = k & 1;
+                // slot k % 2 is free once every reader of item k-2 is done with it
+                if (k >= 2 && !mbar_wait(bItemEmpty(slot), ((k >> 1) - 1) & 1, abort_flag, status)) break;
+                const int w = atomicAdd(sched, 1);
+                const ItemGeo it = item_geo(w < n_items ? w : 0, n_pairs, Hq, S, causal, window, key_len);
+                publish_item(slots + kSlotInts * slot, w < n_items, it, causal, window);
+                mbar_arrive(bItemFull(slot));  // release: the slot's values are visible to the waiters
+                if (w >= n_items) break;
+                const int kvh = it.h / G;
+                bool ok = true;
+                for (int t = 0; t < 2 && ok; ++t) {
+                    if (k >= 1 && !mbar_wait(bQempty(t), (k - 1) & 1, abort_flag, status)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(bQfull(t), Gm::kTileBytes);
                     for (int pn = 0; pn < NP; ++pn)
-                        tma_load_4d(sK + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmK, bKVfull(st), 64 * pn, kvh,
-                                    (t_begin + i) * kBN, b);
-                if (has_v)
-                    for (int pn = 0; pn < NP; ++pn)
-                        tma_load_4d(sV + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmV, bKVfull(st), 64 * pn, kvh,
-                                    (t_begin + i - 1) * kBN, b);
-                issued = i + 1;
+                        tma_load_4d(sQ + t * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmQ, bQfull(t), 64 * pn, it.h,
+                                    t ? it.q0b : it.q0a, it.b);
+                }
+                if (!ok) break;
+                q_items = k + 1;
+                // ring items 0..n_max of this work item (n_max >= 1), each into its stage after
+                // the stage's previous ring item was released
+                for (int i = 0; i <= it.n_max; ++i) {
+                    const int st = g % ST;
+                    if (g >= ST && !mbar_wait(bKVempty(st), ((g / ST) - 1) & 1, abort_flag, status)) {
+                        ok = false;
+                        break;
+                    }
+                    const bool has_k = i < it.n_max, has_v = i >= 1;
+                    mbar_expect_tx(bKVfull(st), (has_k ? Gm::kTxTile : 0u) + (has_v ? Gm::kTxTile : 0u));
+                    if (has_k)
+                        for (int pn = 0; pn < NP; ++pn)
+                            tma_load_4d(sK + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmK, bKVfull(st), 64 * pn,
+                                        kvh, (it.t_begin + i) * kBN, it.b);
+                    if (has_v)
+                        for (int pn = 0; pn < NP; ++pn)
+                            tma_load_4d(sV + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmV, bKVfull(st), 64 * pn,
+                                        kvh, (it.t_begin + i - 1) * kBN, it.b);
+                    ++g;
+                }
+                if (!ok) break;
             }
             // every copy this thread issued lands before the CTA may exit
-            mbar_drain(bQ, 0);
-            for (int i = (issued > ST ? issued - ST : 0); i < issued; ++i) mbar_drain(bKVfull(i % ST), (i / ST) & 1);
+            if (q_items > 0)
+                for (int t = 0; t < 2; ++t) mbar_drain(bQfull(t), (q_items - 1) & 1);
+            for (int i = (g > ST ? g - ST : 0); i < g; ++i) mbar_drain(bKVfull(i % ST), (i / ST) & 1);
         }
     } else if (warp == 9) {
         // ------------------------------------------------------------ MMA issuer
@@ -463,10 +571,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         // issues the MMAs and commits.
         {
             const uint32_t ln = (uint32_t)lane;
-            const uint32_t idq = make_idesc(p.fmt, kBM, kBN, 0, 0);
-            const uint32_t idp = make_idesc(p.fmt, kBM, D, 0, 1);
-            int item_ready = -1;  // highest ring item whose full wait was observed
-            bool ok = __all_sync(0xffffffffu, mbar_wait(bQ, 0, abort_flag, status));
+            // fp16 operands (attn_tcgen05_supported), fp32 accumulators
+            constexpr uint32_t idq = make_idesc(0, kBM, kBN, 0, 0);
+            constexpr uint32_t idp = make_idesc(0, kBM, D, 0, 1);
+            int g = 0;                // ring items of earlier work items
+            int item_ready = -1;      // highest ring item whose full wait was observed
+            int cp0 = 0, cp1 = 0;     // P hand-overs consumed per tile
+            bool ok = true;
             auto wait_item = [&](int i) -> bool {
                 if (item_ready >= i) return true;
                 if (!__all_sync(0xffffffffu, mbar_wait(bKVfull(i % ST), (i / ST) & 1, abort_flag, status)))
@@ -481,9 +592,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             const uint64_t dV = smem_desc(sV, Gm::kPanelBytes, 1024);
             const uint32_t q_lo = (uint32_t)dQ, k_lo = (uint32_t)dK, v_lo = (uint32_t)dV;
             const uint32_t qk_hi = (uint32_t)(dQ >> 32), v_hi = (uint32_t)(dV >> 32);  // dK's high word is dQ's
-            auto issue_qk = [&](int t, int j) {
+            // S_t = Q_t K^T with K in ring stage st
+            auto issue_qk = [&](int t, int st) {
                 const uint32_t a0 = q_lo + (uint32_t)(t * Gm::kTileBytes >> 4);
-                const uint32_t b0 = k_lo + (uint32_t)((j % ST) * Gm::kTileBytes >> 4);
+                const uint32_t b0 = k_lo + (uint32_t)(st * Gm::kTileBytes >> 4);
                 const uint32_t d = tmem + 128u * t;
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ++ks) {
@@ -493,47 +605,69 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 }
                 umma_commit_w(ln, bSfull(t));
             };
-            auto issue_pv = [&](int t, int j) {
-                // V(j) (ring item j+1), MN-major: 8-key atoms 1024 B apart (SBO), 64-column panels kPanelBytes
-                // apart (LBO)
-                const uint32_t b0 = v_lo + (uint32_t)(((j + 1) % ST) * Gm::kTileBytes >> 4);
+            // O_t (+)= P_t V with V in ring stage st, MN-major: 8-key atoms 1024 B apart (SBO),
+            // 64-column panels kPanelBytes apart (LBO)
+            auto issue_pv = [&](int t, int st, uint32_t acc) {
+                const uint32_t b0 = v_lo + (uint32_t)(st * Gm::kTileBytes >> 4);
                 const uint32_t d = tmem + 256u + 128u * t, a = tmem + 128u * t;
-                umma_ts_w<-1>(ln, d, a, b0, v_hi, idp, j > 0 ? 1u : 0u);
+                umma_ts_w<-1>(ln, d, a, b0, v_hi, idp, acc);
 #pragma unroll
                 for (int kk = 1; kk < kBN / 16; ++kk) umma_ts_w<1>(ln, d, a + kk * 8u, b0 + kk * 128u, v_hi, idp);
             };
-            if (ok && n_max > 0) {
-                ok = wait_item(0);
-                if (ok && nt0 > 0) issue_qk(0, 0);
-                if (ok && nt1 > 0) issue_qk(1, 0);
-                if (ok) umma_commit_w(ln, bKVempty(0));  // item 0 (K(0)) read by both tiles
-            }
-            for (int j = 0; j < n_max && ok; ++j) {
-                // the tile whose part of this step reads item j+1 last: tile B whenever it takes
-                // part (its rows follow tile A's, so nt0 <= nt1 unless tile B is empty)
-                const int rel = j < nt1 ? 1 : 0;
-                // rolled over the two tiles: unrolled, each tile's per-step descriptor words
-                // would be loop-invariant and hoisted into (spilled) registers
-#pragma unroll 1
-                for (int t = 0; t < 2 && ok; ++t) {
-                    const int ntt = t ? nt1 : nt0;
-                    if (j >= ntt) continue;
-                    if (!__all_sync(0xffffffffu, mbar_wait(bPfull(t), j & 1, abort_flag, status))) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    if (!wait_item(j + 1)) {  // V(j), K(j+1)
-                        ok = false;
-                        break;
-                    }
-                    issue_pv(t, j);
-                    // O_t is complete after its last PV; earlier PVs need no signal of their own:
-                    // S_t(j+1) is committed after PV_t(j), and a commit tracks every earlier MMA
-                    if (j + 1 == ntt) umma_commit_w(ln, bOdone(t));
-                    if (j + 1 < ntt) issue_qk(t, j + 1);
-                    if (t == rel) umma_commit_w(ln, bKVempty((j + 1) % ST));
+            for (int k = 0; ok; ++k) {
+                const int slot = k & 1;
+                if (!__all_sync(0xffffffffu, mbar_wait(bItemFull(slot), (k >> 1) & 1, abort_flag, status))) {
+                    ok = false;
+                    break;
                 }
+                volatile int* const ms = slots + kSlotInts * slot;
+                if (!ms[kSlotValid]) break;
+                const int nt0 = ms[kSlotNt0], nt1 = ms[kSlotNt1], n_max = max(nt0, nt1);
+                ok = __all_sync(0xffffffffu, mbar_wait(bQfull(0), k & 1, abort_flag, status) &&
+                                                 mbar_wait(bQfull(1), k & 1, abort_flag, status));
+                if (ok) ok = wait_item(g);
+                if (!ok) break;
+                // S_t(0); a tile with at most one key tile reads Q_t for the last time here
+                if (nt0 > 0) issue_qk(0, g % ST);
+                if (nt0 <= 1) umma_commit_w(ln, bQempty(0));
+                if (nt1 > 0) issue_qk(1, g % ST);
+                if (nt1 <= 1) umma_commit_w(ln, bQempty(1));
+                umma_commit_w(ln, bKVempty(g % ST));  // ring item 0 (K(0)) read by both tiles
+                for (int j = 0; j < n_max && ok; ++j) {
+                    const int st = (g + j + 1) % ST;  // ring item j+1: V(j), K(j+1)
+                    // the tile whose part of this step reads ring item j+1 last: tile B whenever it
+                    // takes part (its rows follow tile A's, so nt0 <= nt1 unless tile B is empty)
+                    const int rel = j < nt1 ? 1 : 0;
+                    // rolled over the two tiles: unrolled, each tile's per-step descriptor words
+                    // would be loop-invariant and hoisted into (spilled) registers
+#pragma unroll 1
+                    for (int t = 0; t < 2 && ok; ++t) {
+                        const int ntt = t ? nt1 : nt0;
+                        if (j >= ntt) continue;
+                        const int cp = t ? cp1++ : cp0++;
+                        if (!__all_sync(0xffffffffu, mbar_wait(bPfull(t), cp & 1, abort_flag, status))) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        if (!wait_item(g + j + 1)) {
+                            ok = false;
+                            break;
+                        }
+                        issue_pv(t, st, j > 0 ? 1u : 0u);
+                        // O_t is complete after its last PV; earlier PVs need no signal of their own:
+                        // S_t(j+1) is committed after PV_t(j), and a commit tracks every earlier MMA
+                        if (j + 1 == ntt) umma_commit_w(ln, bOdone(t));
+                        if (j + 1 < ntt) {
+                            issue_qk(t, st);
+                            if (j + 2 == ntt) umma_commit_w(ln, bQempty(t));  // the item's last QK of tile t
+                        }
+                        if (t == rel) umma_commit_w(ln, bKVempty(st));
+                    }
+                }
+                g += n_max + 1;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bItemEmpty(slot));  // done with the slot
             }
             // all MMAs lane 0 issued are complete before TMEM is released
             umma_commit_w(ln, bDrain);
@@ -545,78 +679,123 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         // ------------------------------------------------------------ softmax groups
         const int t = warp >> 2;       // 0: tile A, 1: tile B
         const int row = tid & 127;     // TMEM lane within the group
-        // this group's tile bounds as scalars (no dynamically indexed arrays in the hot loop)
-        const int my_q0 = t ? q0t[1] : q0t[0];
-        const int my_kb = t ? kb[1] : kb[0];
-        const int my_ke = t ? ke[1] : ke[0];
-        const int my_nt = t ? nt[1] : nt[0];
-        const int q = my_q0 + row;
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const uint32_t s_addr = lane_base + (t ? 128u : 0u);
         const uint32_t o_addr = lane_base + (t ? 384u : 256u);
+        const int S = p.S, causal = p.causal, window = p.window;
+        const float* const mask = kAdditive ? p.mask : nullptr;
+        const float scale = p.scale;
         const float sl2 = p.scale_log2;
-        const int q_lo = my_q0, q_hi = my_q0 + kBM - 1;
-        // keys this row sees: [row_lo, row_hi); a uniform row (no valid key) weights all keys equally
-        int row_lo = my_kb, row_hi = my_ke;
-        if (causal) {
-            row_hi = min(row_hi, q + 1);
-            if (window > 0) row_lo = max(row_lo, q - window + 1);
-        }
-        const float edge_mult = uniform ? 0.f : sl2;
-        const bool additive = kAdditive && !uniform;
-        float m_run = -INFINITY, l_run = 0.f;
+        int cs = 0, co = 0;  // S and O hand-overs consumed
         bool ok = true;
-        for (int j = 0; j < my_nt && ok; ++j) {
-            if (!__all_sync(0xffffffffu, mbar_wait(bSfull(t), j & 1, abort_flag, status))) {
+        for (int k = 0; ok; ++k) {
+            const int slot = k & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(bItemFull(slot), (k >> 1) & 1, abort_flag, status))) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
-            const int n0 = (t_begin + j) * kBN;
-            // a tile needs per-element masks when it touches the diagonal, the window start or the key end
-            const bool edge = uniform || kAdditive || n0 + kBN > my_ke || n0 < my_kb ||
-                              (causal && n0 + kBN - 1 > q_lo) || (causal && window > 0 && n0 <= q_hi - window);
-            // the whole score row in registers: one TMEM read serves both passes
-            uint32_t r[kBN];
-#pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) tmem_ld32(s_addr + 32 * c, r + 32 * c);
-            tmem_wait_ld();
-            if (edge) {
-                // masked tiles become log2-domain scores (-inf outside the row's keys)
-                const int lo = row_lo - n0, hi = row_hi - n0;
-                if (additive) {
-                    const float* mrow = mask + (int64_t)b * S + n0;
-#pragma unroll
-                    for (int i = 0; i < kBN; ++i)
-                        r[i] = __float_as_uint(i >= lo && i < hi
-                                                   ? (__uint_as_float(r[i]) * scale + __ldg(mrow + i)) * kLog2e
-                                                   : -INFINITY);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < kBN; ++i)
-                        r[i] = __float_as_uint(i >= lo && i < hi ? __uint_as_float(r[i]) * edge_mult : -INFINITY);
+            volatile int* const ms = slots + kSlotInts * slot;
+            if (!ms[kSlotValid]) break;
+            // this group's tile: key tiles, visible keys per row, interior key-tile starts
+            const int my_nt = ms[t ? kSlotNt1 : kSlotNt0];
+            const int q = ms[t ? kSlotQ0b : kSlotQ0a] + row;
+            const int n_base = ms[kSlotTBegin] * kBN;
+            // keys this row sees: [row_lo, row_hi); a uniform row (no valid key) weights all keys equally
+            int row_lo = ms[t ? kSlotKb1 : kSlotKb0], row_hi = ms[t ? kSlotKe1 : kSlotKe0];
+            if (causal) {
+                row_hi = min(row_hi, q + 1);
+                if (window > 0) row_lo = max(row_lo, q - window + 1);
+            }
+            // key tiles starting in [int_lo, int_hi] need no per-element mask
+            const int int_lo = ms[t ? kSlotIntLo1 : kSlotIntLo0], int_hi = ms[t ? kSlotIntHi1 : kSlotIntHi0];
+            const bool uniform = ms[kSlotUniform] != 0;
+            const float* const mrow0 = kAdditive ? mask + (int64_t)ms[kSlotB] * S : nullptr;
+            const float edge_mult = uniform ? 0.f : sl2;
+            const bool additive = kAdditive && !uniform;
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < my_nt; ++j) {
+                if (!__all_sync(0xffffffffu, mbar_wait(bSfull(t), cs & 1, abort_flag, status))) {
+                    ok = false;
+                    break;
                 }
-            }
-            // pass 1: row maximum (raw scores on interior tiles, scaled after)
-            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+                ++cs;
+                tc_fence_after();
+                const int n0 = n_base + j * kBN;
+                // a tile needs per-element masks when it touches the diagonal, the window start or the key end
+                const bool edge = kAdditive || n0 < int_lo || n0 > int_hi;
+                // the whole score row in registers: one TMEM read serves both passes
+                uint32_t r[kBN];
 #pragma unroll
-            for (int i = 0; i < kBN; i += 8) {
-                mx0 = max3f(mx0, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-                mx1 = max3f(mx1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-                mx2 = max3f(mx2, __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
-                mx3 = max3f(mx3, __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
-            }
-            float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-            if (!edge) mx *= sl2;
-            // lazy rescale: move the reference maximum only when it grew by > threshold
-            const bool need = mx > m_run + kRescaleThreshold;
-            if (__any_sync(0xffffffffu, need)) {
-                const float m_new = need ? mx : m_run;
-                const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
-                l_run *= alpha;
-                // O_t holds PV(j-1) complete: S_t(j), waited for above, was committed after it
-                if (j > 0) {
+                for (int c = 0; c < kBN / 32; ++c) tmem_ld32(s_addr + 32 * c, r + 32 * c);
+                tmem_wait_ld();
+                if (edge) {
+                    // masked tiles become log2-domain scores (-inf outside the row's keys)
+                    const int lo = row_lo - n0, hi = row_hi - n0;
+                    if (additive) {
+                        const float* mrow = mrow0 + n0;
 #pragma unroll
+                        for (int i = 0; i < kBN; ++i)
+                            r[i] = __float_as_uint(i >= lo && i < hi
+                                                       ? (__uint_as_float(r[i]) * scale + __ldg(mrow + i)) * kLog2e
+                                                       : -INFINITY);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < kBN; ++i)
+                            r[i] = __float_as_uint(i >= lo && i < hi ? __uint_as_float(r[i]) * edge_mult : -INFINITY);
+                    }
+                }
+                // pass 1: row maximum (raw scores on interior tiles, scaled after)
+                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+                for (int i = 0; i < kBN; i += 8) {
+                    mx0 = max3f(mx0, __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+                    mx1 = max3f(mx1, __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+                    mx2 = max3f(mx2, __uint_as_float(r[i + 4]), __uint_as_float(r[i + 5]));
+                    mx3 = max3f(mx3, __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
+                }
+                float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+                if (!edge) mx *= sl2;
+                // lazy rescale: move the reference maximum only when it grew by > threshold;
+                // O is multiplied after pass 2, when the score row no longer holds registers
+                const bool need = mx > m_run + kRescaleThreshold;
+                const bool rescale = __any_sync(0xffffffffu, need);
+                float alpha = 1.f;
+                if (rescale) {
+                    const float m_new = need ? mx : m_run;
+                    alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
+                    l_run *= alpha;
+                    m_run = m_new;
+                }
+                const float mb = m_run == -INFINITY ? 0.f : m_run;
+                // pass 2: P = 2^(s - m) as fp16 pairs over the first 64 S columns, row sum
+                const float mul = edge ? 1.f : sl2;
+                const f32x2 mul2 = f2_make(mul, mul), nmb2 = f2_make(-mb, -mb);
+                f32x2 sum0 = 0ull, sum1 = 0ull;
+                uint32_t pk[kBN / 2];
+#pragma unroll
+                for (int i = 0; i < kBN; i += 2) {
+                    float x0, x1, e0, e1;
+                    f2_split(f2_fma(f2_make(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), mul2, nmb2), x0, x1);
+                    // kPolyPairs of every 8 pairs on the FMA pipe, the rest on the MUFU
+                    if (((i >> 1) & 7) >= 8 - kPolyPairs) {
+                        exp2_poly_pair(x0, x1, e0, e1);
+                    } else {
+                        e0 = fast_exp2(x0);
+                        e1 = fast_exp2(x1);
+                    }
+                    if ((i >> 1) & 1) sum1 = f2_add(sum1, f2_make(e0, e1));
+                    else sum0 = f2_add(sum0, f2_make(e0, e1));
+                    pk[i >> 1] = pack_half2(e0, e1);
+                    if (((i >> 1) & 15) == 15) tmem_st16(s_addr + (uint32_t)((i >> 1) - 15), pk + (i >> 1) - 15);
+                }
+                float a0, a1, b0, b1;
+                f2_split(sum0, a0, a1);
+                f2_split(sum1, b0, b1);
+                l_run += (a0 + a1) + (b0 + b1);
+                // O_t holds PV(j-1) complete: S_t(j), waited for above, was committed after it;
+                // PV(j) adds to O only after the hand-over below
+                if (rescale && j > 0) {
+#pragma unroll 1
                     for (int c = 0; c < D / 32; ++c) {
                         uint32_t o[32];
                         tmem_ld32(o_addr + 32 * c, o);
@@ -626,64 +805,57 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                         tmem_st32(o_addr + 32 * c, o);
                     }
                 }
-                m_run = m_new;
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(bPfull(t));
             }
-            const float mb = m_run == -INFINITY ? 0.f : m_run;
-            // pass 2: P = 2^(s - m) as fp16 pairs over the first 64 S columns, row sum
-            const float mul = edge ? 1.f : sl2;
-            const f32x2 mul2 = f2_make(mul, mul), nmb2 = f2_make(-mb, -mb);
-            f32x2 sum0 = 0ull, sum1 = 0ull;
-            uint32_t pk[kBN / 2];
-#pragma unroll
-            for (int i = 0; i < kBN; i += 2) {
-                float x0, x1, e0, e1;
-                f2_split(f2_fma(f2_make(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), mul2, nmb2), x0, x1);
-                // kPolyPairs of every 8 pairs on the FMA pipe, the rest on the MUFU
-                if (((i >> 1) & 7) >= 8 - kPolyPairs) {
-                    exp2_poly_pair(x0, x1, e0, e1);
-                } else {
-                    e0 = fast_exp2(x0);
-                    e1 = fast_exp2(x1);
+            // epilogue: O / l for rows inside the sequence.  O_t is read out (tcgen05.ld, waited
+            // for) before this group hands over the next item's first P, the point after which
+            // that item's first PV overwrites O_t.
+            if (!ok) break;
+            if (my_nt > 0) {
+                if (!__all_sync(0xffffffffu, mbar_wait(bOdone(t), co & 1, abort_flag, status))) {
+                    ok = false;
+                    break;
                 }
-                if ((i >> 1) & 1) sum1 = f2_add(sum1, f2_make(e0, e1));
-                else sum0 = f2_add(sum0, f2_make(e0, e1));
-                pk[i >> 1] = pack_half2(e0, e1);
-                if (((i >> 1) & 15) == 15) tmem_st16(s_addr + (uint32_t)((i >> 1) - 15), pk + (i >> 1) - 15);
-            }
-            float a0, a1, b0, b1;
-            f2_split(sum0, a0, a1);
-            f2_split(sum1, b0, b1);
-            l_run += (a0 + a1) + (b0 + b1);
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(bPfull(t));
-        }
-        // epilogue: O / l for rows inside the sequence
-        if (ok && my_nt > 0 && __all_sync(0xffffffffu, mbar_wait(bOdone(t), 0, abort_flag, status))) {
-            tc_fence_after();
-            const float inv = 1.f / l_run;
+                ++co;
+                tc_fence_after();
+                const float inv = 1.f / l_run;
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(o_addr + 32 * c, r);
-                tmem_wait_ld();
-                if (q < S) {
-                    const int64_t off = b * p.o_sb + (int64_t)q * p.o_ss + h * p.o_sh + 32 * c;
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(o_addr + 32 * c, r);
+                    tmem_wait_ld();
+                    if (q < S) {
+                        const int64_t off = ms[kSlotB] * p.o_sb + (int64_t)q * p.o_ss + ms[kSlotH] * p.o_sh + 32 * c;
 #pragma unroll
-                    for (int i = 0; i < 32; i += 8) {
-                        float v[8];
+                        for (int i = 0; i < 32; i += 8) {
+                            float v[8];
 #pragma unroll
-                        for (int k = 0; k < 8; ++k) v[k] = __uint_as_float(r[i + k]) * inv;
-                        store8(p.out, off + i, v, p.out_dtype);
+                            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[i + e]) * inv;
+                            store8(p.out, off + i, v, p.out_dtype);
+                        }
                     }
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bItemEmpty(slot));  // done with the slot
         }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    // the last CTA to finish resets the work-item counters for the next launch: every CTA
+    // has fetched its last item (its producer is past the barrier above) before it counts
+    if (tid == 0) {
+        int* const sched = p.sched;
+        __threadfence();
+        if (atomicAdd(sched + 1, 1) == (int)gridDim.x - 1) {
+            atomicExch(sched, 0);
+            atomicExch(sched + 1, 0);
+        }
+    }
 }
 
 // ---------------------------------------------------------------- host side
@@ -754,6 +926,9 @@ cudaError_t kernel_ready_for(const AttnParams& p) {
     return p.mask != nullptr ? kernel_ready<D, true>() : kernel_ready<D, false>();
 }
 
+// query-tile pairs x heads x batch
+int64_t work_items(const AttnParams& a) { return (int64_t)((a.S + 2 * kBM - 1) / (2 * kBM)) * a.Hq * a.B; }
+
 template <int D>
 cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream) {
     const bool additive = a.mask != nullptr;
@@ -785,7 +960,14 @@ cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream) {
     p.o_sh = a.q_sh;
     p.status = status;
     p.fmt = fmt;
-    dim3 grid((a.S + 2 * kBM - 1) / (2 * kBM), a.Hq, a.B);
+    // persistent: one CTA per SM (each holds all of TMEM), work items from the counter
+    p.sched = status + kStatusSchedWord;
+    p.n_items = (int)work_items(a);
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                  cudaSuccess || sms <= 0)
+        return cudaErrorInvalidDevice;
+    const dim3 grid((unsigned)std::min(p.n_items, sms));
     if (additive)
         attn_tcgen05_kernel<D, true><<<grid, kThreadsTc, smem_request<D>(), stream>>>(mq, mk, mv, p);
     else
@@ -805,7 +987,8 @@ bool attn_tcgen05_supported(const AttnParams& p) {
     const uintptr_t ptrs[] = {(uintptr_t)p.q, (uintptr_t)p.k, (uintptr_t)p.v, (uintptr_t)p.o};
     for (uintptr_t x : ptrs)
         if (x % 16 != 0) return false;
-    if (p.Hq > 65535 || p.B > 65535 || encode_fn() == nullptr) return false;
+    // the work-item counter reaches items + grid within int32
+    if (p.Hq > 65535 || p.B > 65535 || work_items(p) > INT32_MAX / 2 || encode_fn() == nullptr) return false;
     const cudaError_t ready = p.D == 64 ? kernel_ready_for<64>(p) : p.D == 96 ? kernel_ready_for<96>(p)
                                                                                : kernel_ready_for<128>(p);
     return ready == cudaSuccess;

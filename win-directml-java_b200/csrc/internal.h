@@ -96,7 +96,16 @@ struct AttnParams {
 };
 
 cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t stream);
+// The context's device status buffer: words [0, kStatusWords) are the error flags
+// b2a_check_device_status reports and clears; words kStatusSchedWord and the next one are
+// the persistent prefill kernel's work-item counters (zero between launches: the last CTA
+// of each launch resets them).
+constexpr int kStatusWords = 4;
+constexpr int kStatusSchedWord = 4;
+constexpr int kStatusBufferInts = 8;
+
 // tcgen05 / TMEM / TMA kernel (fp16 operands, head_dim 64, 96, 128); status bit 3 = bounded wait ran out.
+// `status` is the context's status buffer (kStatusBufferInts ints).
 bool attn_tcgen05_supported(const AttnParams& p);
 cudaError_t launch_attn_tcgen05(const AttnParams& p, int* status, cudaStream_t stream);
 bool attn_tc_supported(const AttnParams& p);
