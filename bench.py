@@ -378,7 +378,7 @@ def run_suite(ctx, hbm, tflops, src):
 
     def flush():
         flush_buf.fill_(1.0)
-        torch.sum(clean_buf, out=clean_sum)
+        torch.sum(clean_buf, dim=0, out=clean_sum)
     out = {}
     for name in ("c1", "c2", "c3", "c4"):
         w = DecodeWorkload(name, 3) if name == "c3" else PrefillWorkload(name, {"c1": 1, "c2": 2, "c4": 4}[name])
