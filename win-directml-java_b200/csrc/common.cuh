@@ -16,6 +16,18 @@ __device__ __forceinline__ float load_as_float(const void* p, int64_t i, int dty
     return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
 }
 
+// The element's bits, not yet converted: a load whose value is used only later, so that
+// its latency can overlap other work (raw_to_float converts it then).
+__device__ __forceinline__ uint32_t load_raw(const void* p, int64_t i, int dtype) {
+    if (dtype == kF32) return __ldg(static_cast<const unsigned int*>(p) + i);
+    return __ldg(static_cast<const unsigned short*>(p) + i);
+}
+__device__ __forceinline__ float raw_to_float(uint32_t r, int dtype) {
+    if (dtype == kF32) return __uint_as_float(r);
+    if (dtype == kF16) return __half2float(__ushort_as_half((unsigned short)r));
+    return __bfloat162float(__ushort_as_bfloat16((unsigned short)r));
+}
+
 __device__ __forceinline__ void store_from_float(void* p, int64_t i, float v, int dtype) {
     if (dtype == kF32) static_cast<float*>(p)[i] = v;
     else if (dtype == kF16) static_cast<__half*>(p)[i] = __float2half_rn(v);

@@ -68,8 +68,6 @@ struct Geo {
     static constexpr size_t kPrefixBytes = size_t(kDecodeMaxBatchPerLaunch + 1) * 4;
     static constexpr size_t kMlBytes = size_t(kWarps) * kHeads * 2 * 4;
     static constexpr size_t kMergeBytes = size_t(kWarps) * kHeads * D * 4;  // aliases the pipe
-    // merge weights [pieces][kHeads] + [kHeads] sums also alias the pipe
-    static constexpr int kMaxPieces = int((kPipeBytes - kMergeBytes) / (kHeads * 4)) - 1;
     static_assert(kMergeBytes <= kPipeBytes, "merge scratch must fit in the pipeline buffers");
     // every region starts on a 16-byte boundary (misc is read as 8-byte words,
     // cs as doubles, the pipe and q rows by 16-byte cp.async / ldmatrix)
@@ -80,15 +78,24 @@ struct Geo {
     static constexpr size_t oVec = a16(oNew + kNewBytes);
     static constexpr size_t oCs = a16(oVec + kVecBytes);
     static constexpr size_t oPrefix = a16(oCs + kCsBytes);
-    static constexpr size_t oMl = a16(oPrefix + kPrefixBytes);
+    // context length per sequence, cached by the plan for the piece loop where it fits
+    // (every head dim but 256, whose pipeline fills shared memory)
+    static constexpr size_t kLensBytes = size_t(kDecodeMaxBatchPerLaunch) * 4;
+    static constexpr size_t oLens = a16(oPrefix + kPrefixBytes);
+    static constexpr bool kLensCached = a16(oLens + kLensBytes) + kMlBytes + 64 <= 227 * 1024;
+    static constexpr size_t oMl = kLensCached ? a16(oLens + kLensBytes) : oLens;
     static constexpr size_t oMisc = a16(oMl + kMlBytes);
     static constexpr size_t kTotal = oMisc + 64;
     static_assert(oMisc % 16 == 0 && oCs % 16 == 0 && oMl % 16 == 0, "aligned shared regions");
     static_assert(kTotal <= 227 * 1024, "shared memory budget");
 };
 
-__device__ __forceinline__ bool seq_range(const DecodeParams& p, int b, int& L, int& first) {
-    L = p.ctx_lens ? p.ctx_lens[b] : p.pos_scalar;
+__device__ __forceinline__ int ctx_len_of(const DecodeParams& p, int b) {
+    return p.ctx_lens ? p.ctx_lens[b] : p.pos_scalar;
+}
+// Visible key range [first, L] of a sequence whose context length is L_in.
+__device__ __forceinline__ bool seq_range_of(const DecodeParams& p, int L_in, int& L, int& first) {
+    L = L_in;
     if (L < 0 || L >= p.max_seq) {
         L = 0;
         first = 0;
@@ -99,6 +106,9 @@ __device__ __forceinline__ bool seq_range(const DecodeParams& p, int b, int& L, 
     else first = 0;
     return true;
 }
+__device__ __forceinline__ bool seq_range(const DecodeParams& p, int b, int& L, int& first) {
+    return seq_range_of(p, ctx_len_of(p, b), L, first);
+}
 
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
@@ -106,18 +116,35 @@ __device__ __forceinline__ double warp_sum_d(double v) {
     return v;
 }
 
-// Loads one head vector, applies the optional QK-norm, and writes it (rotated
-// when requested) as float into vec[0..D).  Whole warp; vec is warp-private.
+// One head vector's elements d = lane + 32 j as loaded (raw bits) and its optional
+// projection bias, requested early and converted later by prep_finish.
 template <int D>
-__device__ __forceinline__ void prep_head(const DecodeParams& p, const void* src, int64_t off, int dtype,
-                                          const float* bias, const float* norm_w, bool rope, const double* cs,
-                                          float* vec, int lane) {
+struct HeadLoad {
+    uint32_t raw[D / 32];
+    float bias[D / 32];
+};
+template <int D>
+__device__ __forceinline__ void head_load(HeadLoad<D>& h, const void* src, int64_t off, int dtype, const float* bias,
+                                          int lane) {
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) {
+        h.raw[j] = load_raw(src, off + lane + 32 * j, dtype);
+        h.bias[j] = bias != nullptr ? __ldg(bias + lane + 32 * j) : 0.f;
+    }
+}
+
+// Converts a loaded head vector, adds its bias, applies the optional QK-norm, and
+// writes it (rotated when requested) as float into vec[0..D).  Whole warp; vec is
+// warp-private.
+template <int D>
+__device__ __forceinline__ void prep_finish(const DecodeParams& p, const HeadLoad<D>& h, int dtype, bool has_bias,
+                                            const float* norm_w, bool rope, const double* cs, float* vec, int lane) {
     double ss = 0.0;
     float x[D / 32];
 #pragma unroll
     for (int j = 0; j < D / 32; ++j) {
-        x[j] = load_as_float(src, off + lane + 32 * j, dtype);
-        if (bias != nullptr) x[j] = __fadd_rn(x[j], bias[lane + 32 * j]);  // projection bias, fp32
+        x[j] = raw_to_float(h.raw[j], dtype);
+        if (has_bias) x[j] = __fadd_rn(x[j], h.bias[j]);  // projection bias, fp32
         ss += (double)x[j] * (double)x[j];
     }
     if (norm_w != nullptr) {
@@ -187,6 +214,7 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
     float* vec_all = reinterpret_cast<float*>(smem + Gm::oVec);
     double* cs_s = reinterpret_cast<double*>(smem + Gm::oCs);
     int* prefix = reinterpret_cast<int*>(smem + Gm::oPrefix);
+    int* lens_s = reinterpret_cast<int*>(smem + Gm::oLens);  // valid when Gm::kLensCached
     float* ml_s = reinterpret_cast<float*>(smem + Gm::oMl);
     int* misc = reinterpret_cast<int*>(smem + Gm::oMisc);
     float* merge_s = reinterpret_cast<float*>(smem);
@@ -209,8 +237,10 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         const int b0 = min(p.B, tid * per), b1 = min(p.B, b0 + per);
         int run = 0, bad = 0;
         for (int b = b0; b < b1; ++b) {
+            const int L_in = ctx_len_of(p, b);
+            if (Gm::kLensCached) lens_s[b] = L_in;
             int L, first;
-            if (!seq_range(p, b, L, first)) bad = 1;
+            if (!seq_range_of(p, L_in, L, first)) bad = 1;
             run += L - first + 1 + Gm::kGapKeys;
         }
         if (bad && blockIdx.x == 0) atomicOr(p.status, 1);
@@ -228,7 +258,7 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         for (int b = b0; b < b1; ++b) {
             prefix[b] = acc;
             int L, first;
-            seq_range(p, b, L, first);
+            seq_range_of(p, Gm::kLensCached ? lens_s[b] : ctx_len_of(p, b), L, first);
             acc += L - first + 1 + Gm::kGapKeys;
         }
         if (tid == kThreads - 1) prefix[p.B] = warp_off + incl;
@@ -243,6 +273,7 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
     }
     const float scale_log2 = p.scale * kLog2e;
     constexpr float kNegInf = -INFINITY;
+    const bool small = total <= (long long)INT32_MAX;
     const long long range_lo = (long long)blockIdx.x * R;
     const long long range_hi = min(total, range_lo + R);
 
@@ -256,11 +287,12 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         }
         const int b = lo;
         int L, first;
-        const bool ok = seq_range(p, b, L, first);
+        const bool ok = seq_range_of(p, Gm::kLensCached ? lens_s[b] : ctx_len_of(p, b), L, first);
         const int n_b = L - first + 1;
         const int n_v = n_b + Gm::kGapKeys;  // the unit's stream length
         const long long seq_base = (long long)prefix[b] * per_chunk;
-        const int r = (int)((pos - seq_base) / n_v);
+        // 32-bit divisions when the whole stream fits (`small`)
+        const int r = small ? (int)(pos - seq_base) / n_v : (int)((pos - seq_base) / n_v);
         const long long u_start = seq_base + (long long)r * n_v, u_end = u_start + n_b;
         if (pos >= u_end) {  // in the unit's gap: nothing to attend
             pos = u_start + n_v;
@@ -270,7 +302,8 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         const int kvh = r / p.n_hg, hg = r - kvh * p.n_hg;
         const int k0 = first + (int)(pos - u_start);
         const int k1 = first + (int)(piece_end - u_start);
-        const int c0 = (int)(u_start / R), c1 = (int)((u_end - 1) / R);
+        const int c0 = small ? (int)u_start / (int)R : (int)(u_start / R);
+        const int c1 = small ? (int)(u_end - 1) / (int)R : (int)((u_end - 1) / R);
         const int n_split = c1 - c0 + 1;                    // pieces of this unit
         const int my_slot = 2 * blockIdx.x + (pos == range_lo ? 0 : 1);
         const int unit = b * per_chunk + r;
@@ -304,6 +337,31 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
                 cp_async_16(smem_u32(vs + row * kRow + cc * 8), vc + off, in ? 16 : 0);
             }
         };
+
+        // ------------------------------------------------ prologue loads
+        // Every global read of the prologue (RoPE frequencies, this unit's q rows, the new
+        // k/v row, biases) is requested before the first tiles' copies are issued and used
+        // only after them: with HBM saturated by the other CTAs' streams each read takes
+        // microseconds, and issued one after another they were most of a piece's fixed cost.
+        const bool rope = p.append && p.rope_mode != 0;
+        double inv_f = 0.0;
+        if (rope && tid < D / 2) inv_f = __ldg(p.inv_freq + tid);
+        constexpr int kHeadsPerWarp = kHeads / kWarps;
+        static_assert(kHeads % kWarps == 0 && D / 2 <= kThreads, "prologue work split");
+        HeadLoad<D> qload[kHeadsPerWarp];
+#pragma unroll
+        for (int i = 0; i < kHeadsPerWarp; ++i) {
+            const int hl = warp + kWarps * i;
+            if (hl < nh)
+                head_load<D>(qload[i], p.q, (int64_t)b * q_stride_of(p) + (int64_t)(h0 + hl) * D, p.q_dtype,
+                             p.q_bias ? p.q_bias + (h0 + hl) * D : nullptr, lane);
+        }
+        HeadLoad<D> nload;  // warp 0: the new key row, warp 1: the new value row
+        if (has_new && warp < 2)
+            head_load<D>(nload, warp == 0 ? p.k_new : p.v_new, (int64_t)b * kvn_stride_of(p) + (int64_t)kvh * D,
+                         p.q_dtype, warp == 0 ? (p.k_bias ? p.k_bias + kvh * D : nullptr)
+                                              : (p.v_bias ? p.v_bias + kvh * D : nullptr),
+                         lane);
 #pragma unroll
         for (int s = 0; s < kStages - 1; ++s) {
             if (s < n_tiles) load_tile(s, s);
@@ -311,26 +369,24 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         }
 
         // ------------------------------------------------ prologue (q, new k/v)
-        const bool rope = p.append && p.rope_mode != 0;
-        if (rope) {
-            for (int i = tid; i < D / 2; i += kThreads) {
-                double sn, cn;
-                sincos((double)L * p.inv_freq[i], &sn, &cn);
-                cs_s[2 * i] = cn;
-                cs_s[2 * i + 1] = sn;
-            }
+        if (rope && tid < D / 2) {
+            double sn, cn;
+            sincos((double)L * inv_f, &sn, &cn);
+            cs_s[2 * tid] = cn;
+            cs_s[2 * tid + 1] = sn;
         }
         __syncthreads();
-        for (int hl = warp; hl < kHeads; hl += kWarps) {
+#pragma unroll
+        for (int i = 0; i < kHeadsPerWarp; ++i) {
+            const int hl = warp + kWarps * i;
             T* qrow = q_s + hl * kRow;
             T* qlo = qlo_s + hl * kRow;
             if (hl >= nh) {
                 for (int d = lane; d < D; d += 32) qrow[d] = qlo[d] = Elem<T>::from_float(0.f);
                 continue;
             }
-            prep_head<D>(p, p.q, (int64_t)b * q_stride_of(p) + (int64_t)(h0 + hl) * D, p.q_dtype,
-                         p.q_bias ? p.q_bias + (h0 + hl) * D : nullptr, p.append ? p.q_norm_w : nullptr, rope, cs_s,
-                         vec, lane);
+            prep_finish<D>(p, qload[i], p.q_dtype, p.q_bias != nullptr, p.append ? p.q_norm_w : nullptr, rope, cs_s,
+                           vec, lane);
             for (int d = lane; d < D; d += 32) {
                 const T hi = Elem<T>::from_float(vec[d]);
                 qrow[d] = hi;
@@ -340,8 +396,7 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         }
         if (has_new) {
             if (warp == 0) {
-                prep_head<D>(p, p.k_new, (int64_t)b * kvn_stride_of(p) + (int64_t)kvh * D, p.q_dtype,
-                             p.k_bias ? p.k_bias + kvh * D : nullptr, p.k_norm_w, rope, cs_s, vec, lane);
+                prep_finish<D>(p, nload, p.q_dtype, p.k_bias != nullptr, p.k_norm_w, rope, cs_s, vec, lane);
                 T* dst = static_cast<T*>(p.k_cache) + b * p.stride_b + kvh * p.stride_h + (int64_t)L * p.stride_pos;
                 for (int d = lane; d < D; d += 32) {
                     const T v = Elem<T>::from_float(vec[d]);
@@ -350,9 +405,11 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
                 }
             } else if (warp == 1) {
                 T* dst = static_cast<T*>(p.v_cache) + b * p.stride_b + kvh * p.stride_h + (int64_t)L * p.stride_pos;
-                for (int d = lane; d < D; d += 32) {
-                    float vf = load_as_float(p.v_new, (int64_t)b * kvn_stride_of(p) + (int64_t)kvh * D + d, p.q_dtype);
-                    if (p.v_bias != nullptr) vf = __fadd_rn(vf, p.v_bias[kvh * D + d]);
+#pragma unroll
+                for (int j = 0; j < D / 32; ++j) {
+                    const int d = lane + 32 * j;
+                    float vf = raw_to_float(nload.raw[j], p.q_dtype);
+                    if (p.v_bias != nullptr) vf = __fadd_rn(vf, nload.bias[j]);
                     const T v = Elem<T>::from_float(vf);
                     vnew_s[d] = v;
                     if (hg == 0) dst[d] = v;
@@ -522,38 +579,55 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
                 // Last piece of the unit: log-sum-exp combine of its n_split
                 // partial slots.  The piece of CTA c sits in slot 2c, or 2c+1
                 // when the unit starts inside c's range after its first piece.
+                // Each thread combines its own output elements; the loads of up to
+                // kMergeBatch slots are all issued before any is used (one L2 round
+                // trip per batch instead of three dependent ones).
                 __threadfence();
-                float* wgt = merge_s + kWarps * kHeads * D;  // [n_split][kHeads] weights
-                float* lsum = wgt + n_split * kHeads;         // [kHeads]
                 auto slot_of = [&](int c) {
                     const int sub = (c == c0 && u_start != (long long)c0 * R) ? 1 : 0;
                     return p.partials + (int64_t)(2 * c + sub) * kHeads * (D + 2);
                 };
-                for (int e = tid; e < n_split * kHeads; e += kThreads)
-                    wgt[e] = __ldcg(slot_of(c0 + e / kHeads) + kHeads * D + e % kHeads);
-                __syncthreads();
-                if (tid < kHeads) {
-                    float M = kNegInf;
-                    for (int c = 0; c < n_split; ++c) M = fmaxf(M, wgt[c * kHeads + tid]);
-                    float l = 0.f;
-                    for (int c = 0; c < n_split; ++c) {
-                        const float f = fast_exp2(wgt[c * kHeads + tid] - M);
-                        wgt[c * kHeads + tid] = f;
-                        l += f * __ldcg(slot_of(c0 + c) + kHeads * D + kHeads + tid);
-                    }
-                    lsum[tid] = l;
-                }
-                __syncthreads();
                 constexpr int kPer = kHeads * D / kThreads;  // output elements per thread
-                float o[kPer];
+                constexpr int kMergeBatch = kPer <= 4 ? 4 : (kPer <= 8 ? 2 : 1);
+                float o[kPer], lsum[kPer], mrun[kPer];
 #pragma unroll
-                for (int j = 0; j < kPer; ++j) o[j] = 0.f;
-                for (int c = 0; c < n_split; ++c) {
-                    const float* sl = slot_of(c0 + c);
+                for (int j = 0; j < kPer; ++j) {
+                    o[j] = 0.f;
+                    lsum[j] = 0.f;
+                    mrun[j] = kNegInf;
+                }
+                for (int cb = 0; cb < n_split; cb += kMergeBatch) {
+                    float mv[kMergeBatch][kPer], lv[kMergeBatch][kPer], ov[kMergeBatch][kPer];
+#pragma unroll
+                    for (int i = 0; i < kMergeBatch; ++i) {
+                        if (cb + i >= n_split) break;
+                        const float* sl = slot_of(c0 + cb + i);
+#pragma unroll
+                        for (int j = 0; j < kPer; ++j) {
+                            const int e = tid + j * kThreads, hl = e / D;
+                            mv[i][j] = __ldcg(sl + kHeads * D + hl);
+                            lv[i][j] = __ldcg(sl + kHeads * D + kHeads + hl);
+                            ov[i][j] = __ldcg(sl + e);
+                        }
+                    }
 #pragma unroll
                     for (int j = 0; j < kPer; ++j) {
-                        const int e = tid + j * kThreads;
-                        o[j] += wgt[c * kHeads + e / D] * __ldcg(sl + e);
+                        float M = mrun[j];
+#pragma unroll
+                        for (int i = 0; i < kMergeBatch; ++i)
+                            if (cb + i < n_split) M = fmaxf(M, mv[i][j]);
+                        const float base = M == kNegInf ? 0.f : M;
+                        const float keep = fast_exp2(mrun[j] - base);  // 0 for the first batch
+                        o[j] *= keep;
+                        lsum[j] *= keep;
+#pragma unroll
+                        for (int i = 0; i < kMergeBatch; ++i) {
+                            if (cb + i >= n_split) break;
+                            const float f = fast_exp2(mv[i][j] - base);
+                            o[j] += f * ov[i][j];
+                            lsum[j] += f * lv[i][j];
+                        }
+                        mrun[j] = M;
                     }
                 }
 #pragma unroll
@@ -561,7 +635,7 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
                     const int e = tid + j * kThreads;
                     const int hl = e / D, d = e - hl * D;
                     if (hl < nh)
-                        store_from_float(p.out, ((int64_t)b * p.Hq + h0 + hl) * D + d, o[j] / lsum[hl],
+                        store_from_float(p.out, ((int64_t)b * p.Hq + h0 + hl) * D + d, o[j] / lsum[j],
                                          p.out_dtype);
                 }
                 if (tid == 0) *counter = 0;
@@ -589,7 +663,6 @@ LaunchInfo launch_info(int device) {
         if (err == cudaSuccess) err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, info.smem);
         if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
         info.grid = occ * sms;
-        if (info.grid > Geo<D>::kMaxPieces) info.grid = Geo<D>::kMaxPieces;  // merge weights fit in smem
     });
     if (err != cudaSuccess) return LaunchInfo{};
     return info;
