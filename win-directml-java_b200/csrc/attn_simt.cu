@@ -13,8 +13,13 @@
 // coalesced load per tile, shared by all 8 positions and all heads of the
 // group); scores are one key per lane, dot products over fp32 shared rows
 // padded by one word (conflict-free); P·V is lanes over head dimensions with
-// the probabilities broadcast by shuffles.  Online softmax in exp2 with the
-// scale folded in.  q/k arrive already rotated when RoPE applies.
+// the probabilities read back from a per-warp shared row (one broadcast load
+// per key for all heads).  Online softmax in exp2 with the scale folded in.
+// q/k arrive already rotated when RoPE applies.
+// When rows hold whole groups of 4 elements (kVec: head_dim, strides and bases
+// multiples of 4 elements) each thread owns fixed 4-element groups of a tile and
+// loads the next tile's groups into registers while the current tile is used, so a
+// CTA's sequential key tiles do not each wait for a global load.
 #include <math.h>
 
 #include <type_traits>
@@ -32,14 +37,38 @@ constexpr int kTileKeys = 32;                // keys per shared-memory tile (one
 // kHT: query heads per CTA rounded up to 1, 2, 4 or 8; every K and V element read from
 // shared memory feeds all of them (independent FMA chains), padding heads are zeros.
 // kNPL: head dimensions per lane, ceil(D / 32) rounded up to 1, 2, 3, 4 or 8.
-template <int kHT, int kNPL>
+// 4 consecutive elements, not yet converted (16-bit types use the first two words).
+__device__ __forceinline__ uint4 load_raw4(const void* p, int64_t i, int dtype) {
+    if (dtype == kF32) return __ldg(reinterpret_cast<const uint4*>(static_cast<const float*>(p) + i));
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const unsigned short*>(p) + i));
+    return make_uint4(u.x, u.y, 0u, 0u);
+}
+__device__ __forceinline__ void raw4_store(float* dst, uint4 r, int dtype) {
+    if (dtype == kF32) {
+        dst[0] = __uint_as_float(r.x);
+        dst[1] = __uint_as_float(r.y);
+        dst[2] = __uint_as_float(r.z);
+        dst[3] = __uint_as_float(r.w);
+    } else {
+        dst[0] = raw_to_float(r.x & 0xffffu, dtype);
+        dst[1] = raw_to_float(r.x >> 16, dtype);
+        dst[2] = raw_to_float(r.y & 0xffffu, dtype);
+        dst[3] = raw_to_float(r.y >> 16, dtype);
+    }
+}
+
+template <int kHT, int kNPL, bool kVec>
 __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_constant__ AttnParams p, int G) {
     extern __shared__ float sm[];
     const int D = p.D, Dp = D + 1;
     float* ks = sm;                          // [kTileKeys][D + 1]
     float* vs = ks + kTileKeys * Dp;         // [kTileKeys][D + 1]
     float* qs = vs + kTileKeys * Dp;         // [kRows][heads][D]
+    float* ps = qs + kRows * kHT * D;        // [kRows][kTileKeys][kHT] this tile's probabilities
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int in_dtype = p.in_dtype;
+    const float* const mask = p.mask;
+    const int64_t k_ss = p.k_ss;
     const int S = p.S;
     const int s0 = blockIdx.x * kRows;
     const int chunks = (G + kHeads - 1) / kHeads;
@@ -85,22 +114,61 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
         for (int i = 0; i < kNPL; ++i) acc[g][i] = 0.f;
     }
     const int64_t kbase = b * p.k_sb + (int64_t)kvh * p.k_sh;
+    // vector path: this thread's 4-element groups of a tile (key within the tile, first dim);
+    // a tile has kTileKeys * D / 4 <= kNPL * blockDim.x groups
+    constexpr int kG = kVec ? kNPL : 1;
+    int gkey[kG], goff[kG];
+    uint4 kraw[kG], vraw[kG];
+    if constexpr (kVec) {
+        const int G4 = D / 4;
+#pragma unroll
+        for (int i = 0; i < kG; ++i) {
+            const int x = threadIdx.x + i * (kRows * 32);
+            gkey[i] = x < kTileKeys * G4 ? x / G4 : -1;
+            goff[i] = (x % G4) * 4;
+        }
+    }
+    auto fetch = [&](int kb) {  // the tile at kb into registers (zeros past the CTA's last key)
+        const int nk = min(kTileKeys, cta_last - kb + 1);
+#pragma unroll
+        for (int i = 0; i < kG; ++i) {
+            if (gkey[i] >= 0 && gkey[i] < nk) {
+                const int64_t r = kbase + (int64_t)(kb + gkey[i]) * k_ss + goff[i];
+                kraw[i] = load_raw4(p.k, r, in_dtype);
+                vraw[i] = load_raw4(p.v, r, in_dtype);
+            } else {
+                kraw[i] = vraw[i] = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+    };
+    if (kVec && cta_first <= cta_last) fetch(cta_first);
     __syncthreads();
     for (int kb = cta_first; kb <= cta_last; kb += kTileKeys) {
         // stage 32 keys of K and V (fp32) for the whole CTA
         const int nk = min(kTileKeys, cta_last - kb + 1);
-        for (int e = threadIdx.x; e < kTileKeys * D; e += blockDim.x) {
-            const int j = e / D, d = e - j * D;
-            float kv = 0.f, vv = 0.f;
-            if (j < nk) {
-                const int64_t r = kbase + (int64_t)(kb + j) * p.k_ss + d;
-                kv = load_as_float(p.k, r, p.in_dtype);
-                vv = load_as_float(p.v, r, p.in_dtype);
+        if constexpr (kVec) {
+#pragma unroll
+            for (int i = 0; i < kG; ++i) {
+                if (gkey[i] < 0) continue;
+                raw4_store(ks + gkey[i] * Dp + goff[i], kraw[i], in_dtype);
+                raw4_store(vs + gkey[i] * Dp + goff[i], vraw[i], in_dtype);
             }
-            ks[j * Dp + d] = kv;
-            vs[j * Dp + d] = vv;
+        } else {
+            for (int e = threadIdx.x; e < kTileKeys * D; e += blockDim.x) {
+                const int j = e / D, d = e - j * D;
+                float kv = 0.f, vv = 0.f;
+                if (j < nk) {
+                    const int64_t r = kbase + (int64_t)(kb + j) * k_ss + d;
+                    kv = load_as_float(p.k, r, in_dtype);
+                    vv = load_as_float(p.v, r, in_dtype);
+                }
+                ks[j * Dp + d] = kv;
+                vs[j * Dp + d] = vv;
+            }
         }
         __syncthreads();
+        // the next tile's loads are in flight while this one is used
+        if (kVec && kb + kTileKeys <= cta_last) fetch(kb + kTileKeys);
         const int j = kb + lane;
         const bool vis = row_valid && j >= first && j <= last && j - kb < nk;
         const bool any = row_valid && kb <= last && kb + kTileKeys - 1 >= first;
@@ -143,8 +211,8 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
                     }
 #pragma unroll
                     for (int g = 0; g < kHT; ++g)
-                        sc[g] = p.mask != nullptr ? (dot[g] * p.scale + p.mask[(int64_t)b * S + j]) * kLog2e
-                                                  : dot[g] * sl2;
+                        sc[g] = mask != nullptr ? (dot[g] * p.scale + mask[(int64_t)b * S + j]) * kLog2e
+                                                : dot[g] * sl2;
                 }
             }
             float pj[kHT];
@@ -159,10 +227,26 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
 #pragma unroll
                 for (int i = 0; i < kNPL; ++i) acc[g][i] *= corr;
             }
+            // this lane's key's probabilities into the warp's row, read back per key as broadcasts
+            float* prow = ps + warp * kTileKeys * kHT;
+#pragma unroll
+            for (int g = 0; g < kHT; ++g) prow[lane * kHT + g] = pj[g];
+            __syncwarp();
             for (int jj = 0; jj < nk; ++jj) {
                 float pw[kHT];
+                if constexpr (kHT % 4 == 0) {
 #pragma unroll
-                for (int g = 0; g < kHT; ++g) pw[g] = __shfl_sync(0xffffffffu, pj[g], jj);
+                    for (int g = 0; g < kHT; g += 4) {
+                        const float4 t = *reinterpret_cast<const float4*>(prow + jj * kHT + g);
+                        pw[g] = t.x;
+                        pw[g + 1] = t.y;
+                        pw[g + 2] = t.z;
+                        pw[g + 3] = t.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int g = 0; g < kHT; ++g) pw[g] = prow[jj * kHT + g];
+                }
 #pragma unroll
                 for (int i = 0; i < kNPL; ++i) {
                     // dimensions beyond D read the tile's padding (zeros or the next row): their
@@ -196,7 +280,12 @@ cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t stream) {
     const int chunks = (G + kHeads - 1) / kHeads;
     const int heads = G < kHeads ? G : kHeads;
     const int ht = heads <= 1 ? 1 : heads <= 2 ? 2 : heads <= 4 ? 4 : 8;
-    const size_t smem = ((size_t)2 * kTileKeys * (p.D + 1) + (size_t)kRows * ht * p.D) * sizeof(float);
+    const size_t smem =
+        ((size_t)2 * kTileKeys * (p.D + 1) + (size_t)kRows * ht * p.D + (size_t)kRows * kTileKeys * ht) * sizeof(float);
+    // 4-element groups: head dim, strides and bases in whole groups (16 B for fp32, 8 B for 16-bit)
+    const size_t es = p.in_dtype == kF32 ? 4 : 2;
+    const bool vec = p.D % 4 == 0 && p.k_ss % 4 == 0 && p.k_sh % 4 == 0 && p.k_sb % 4 == 0 &&
+                     (uintptr_t)p.k % (4 * es) == 0 && (uintptr_t)p.v % (4 * es) == 0;
     const dim3 grid((p.S + kRows - 1) / kRows, p.Hkv * chunks, p.B);
     auto go = [&](auto kernel) {
         if (smem > 48 * 1024) {
@@ -209,11 +298,15 @@ cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t stream) {
     const int npl = (p.D + 31) / 32;
     auto by_dims = [&](auto ht_tag) {
         constexpr int HT = decltype(ht_tag)::value;
-        if (npl <= 1) return go(attn_simt_kernel<HT, 1>);
-        if (npl <= 2) return go(attn_simt_kernel<HT, 2>);
-        if (npl <= 3) return go(attn_simt_kernel<HT, 3>);
-        if (npl <= 4) return go(attn_simt_kernel<HT, 4>);
-        return go(attn_simt_kernel<HT, 8>);
+        auto pick = [&](auto npl_tag) {
+            constexpr int NPL = decltype(npl_tag)::value;
+            return vec ? go(attn_simt_kernel<HT, NPL, true>) : go(attn_simt_kernel<HT, NPL, false>);
+        };
+        if (npl <= 1) return pick(std::integral_constant<int, 1>{});
+        if (npl <= 2) return pick(std::integral_constant<int, 2>{});
+        if (npl <= 3) return pick(std::integral_constant<int, 3>{});
+        if (npl <= 4) return pick(std::integral_constant<int, 4>{});
+        return pick(std::integral_constant<int, 8>{});
     };
     switch (ht) {
         case 1: return by_dims(std::integral_constant<int, 1>{});
