@@ -93,6 +93,7 @@ def lib() -> ctypes.CDLL:
         L.b2a_workspace_bytes.argtypes = [_vp, ctypes.POINTER(ctypes.c_size_t)]
         L.b2a_reserve_decode.argtypes = [_vp, _i, _i, _i, _i]
         L.b2a_check_device_status.argtypes = [_vp, _vp]
+        L.b2a_test_inject_wait_timeout.argtypes = [_vp]
         L.b2a_mha.argtypes = [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _i, _vp]
         L.b2a_prefill_causal.argtypes = [_vp, _i, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _d, _i, _i,
                                          _vp, _vp]
@@ -108,16 +109,19 @@ def lib() -> ctypes.CDLL:
         for name in ("b2a_create", "b2a_destroy", "b2a_last_error", "b2a_set_workspace_limit", "b2a_workspace_bytes",
                      "b2a_reserve_decode", "b2a_check_device_status", "b2a_mha", "b2a_prefill_causal", "b2a_decode",
                      "b2a_qwen_rope_and_append", "b2a_qwen_gqa_attention_decode", "b2a_qwen_decode_step", "b2a_prefill_gemma",
-                     "b2a_gemma_fused_attention_context", "b2a_partition_units"):
+                     "b2a_gemma_fused_attention_context", "b2a_partition_units", "b2a_test_inject_wait_timeout"):
             getattr(L, name).restype = _i
         _lib = L
         return _lib
 
 
 def declared_symbols() -> list[str]:
-    """Function names declared with B2A_API in include/b200attn.h."""
-    text = open(HEADER_PATH).read()
-    return re.findall(r"B2A_API\s+[\w\s\*]+?\b(b2a_\w+)\s*\(", text)
+    """Function names declared with B2A_API in include/*.h (the boundary and its test hooks)."""
+    import glob
+    names = []
+    for path in sorted(glob.glob(os.path.join(os.path.dirname(HEADER_PATH), "*.h"))):
+        names += re.findall(r"B2A_API\s+[\w\s\*]+?\b(b2a_\w+)\s*\(", open(path).read())
+    return names
 
 
 def _dtype_code(t) -> int:
@@ -193,6 +197,11 @@ class Context:
 
     def check_device_status(self, stream=None):
         self.check(lib().b2a_check_device_status(self._h, _stream(stream)))
+
+    def inject_wait_timeout(self):
+        """Test hook (include/b200attn_testing.h): the next tcgen05 attention launch of this
+        context leaves one K/V copy unissued, so a bounded device wait runs out."""
+        self.check(lib().b2a_test_inject_wait_timeout(self._h))
 
 
 def _message(h) -> str:

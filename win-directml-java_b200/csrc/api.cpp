@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "../../include/b200attn.h"
+#include "../../include/b200attn_testing.h"
 #include "internal.h"
 
 using namespace b2a;
@@ -31,6 +32,9 @@ struct b2a_context {
     // prefill workspace: rope table + rotated q/k staging
     void* pf_ws = nullptr;
     size_t pf_ws_bytes = 0;
+    // test hook (b2a_test_inject_wait_timeout): the next tcgen05 attention launch
+    // leaves one K/V copy unissued
+    bool inject_wait_timeout = false;
 };
 
 namespace {
@@ -115,7 +119,11 @@ int check_head_dim(b2a_context* ctx, int D) {
 // Whole-sequence attention: the tcgen05 kernel where its shape rules hold,
 // else the warp-MMA kernel (16-bit, head_dim 32..128), else the generic one.
 cudaError_t launch_attention(b2a_context* ctx, const AttnParams& p, cudaStream_t s) {
-    if (attn_tcgen05_supported(p)) return launch_attn_tcgen05(p, ctx->status, s);
+    if (attn_tcgen05_supported(p)) {
+        const bool stall = ctx->inject_wait_timeout;
+        ctx->inject_wait_timeout = false;
+        return launch_attn_tcgen05(p, ctx->status, s, stall);
+    }
     if (attn_tc_supported(p)) return launch_attn_tc(p, s);
     return launch_attn_simt(p, s);
 }
@@ -290,6 +298,12 @@ B2A_API int b2a_reserve_decode(b2a_context* ctx, int max_batch, int num_q_heads,
         if (e != cudaSuccess) return cuda_fail(ctx, e, "decode workspace reset");
         ctx->dec_counter_ints = counter_bytes / sizeof(int);
     }
+    return B2A_OK;
+}
+
+B2A_API int b2a_test_inject_wait_timeout(b2a_context* ctx) {
+    if (!ctx) return B2A_EINVAL;
+    ctx->inject_wait_timeout = true;
     return B2A_OK;
 }
 

@@ -87,6 +87,7 @@ struct TcParams {
     int fmt;  // 0 = fp16, 1 = bf16 operands
     int* sched;   // device int[2]: next work item, CTAs finished (zero between launches)
     int n_items;  // work items: query-tile pairs x heads x batch
+    int stall;    // test hook: CTA 0 does not issue ring item 1 (its first item's V(0), K(1))
 };
 
 template <int D>
@@ -515,6 +516,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             int k = 0;        // work items published
             int g = 0;        // ring items issued
             int q_items = 0;  // work items whose Q tiles were issued
+            const int skip_g = (p.stall && blockIdx.x == 0) ? 1 : -1;  // test hook: a copy never issued
             for (;; ++k) {
                 const int slot = k & 1;
                 // slot k % 2 is free once every reader of item k-2 is done with it
@@ -546,6 +548,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                         ok = false;
                         break;
                     }
+                    if (g == skip_g) {  // nothing is issued for it: its consumer's wait runs out
+                        ++g;
+                        continue;
+                    }
                     const bool has_k = i < it.n_max, has_v = i >= 1;
                     mbar_expect_tx(bKVfull(st), (has_k ? Gm::kTxTile : 0u) + (has_v ? Gm::kTxTile : 0u));
                     if (has_k)
@@ -563,7 +569,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             // every copy this thread issued lands before the CTA may exit
             if (q_items > 0)
                 for (int t = 0; t < 2; ++t) mbar_drain(bQfull(t), (q_items - 1) & 1);
-            for (int i = (g > ST ? g - ST : 0); i < g; ++i) mbar_drain(bKVfull(i % ST), (i / ST) & 1);
+            for (int i = (g > ST ? g - ST : 0); i < g; ++i)
+                if (i != skip_g) mbar_drain(bKVfull(i % ST), (i / ST) & 1);
         }
     } else if (warp == 9) {
         // ------------------------------------------------------------ MMA issuer
@@ -930,7 +937,7 @@ cudaError_t kernel_ready_for(const AttnParams& p) {
 int64_t work_items(const AttnParams& a) { return (int64_t)((a.S + 2 * kBM - 1) / (2 * kBM)) * a.Hq * a.B; }
 
 template <int D>
-cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream) {
+cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream, bool stall) {
     const bool additive = a.mask != nullptr;
     const cudaError_t ready = kernel_ready_for<D>(a);
     if (ready != cudaSuccess) return ready;
@@ -963,6 +970,7 @@ cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream) {
     // persistent: one CTA per SM (each holds all of TMEM), work items from the counter
     p.sched = status + kStatusSchedWord;
     p.n_items = (int)work_items(a);
+    p.stall = stall ? 1 : 0;
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
                                                   cudaSuccess || sms <= 0)
@@ -994,11 +1002,11 @@ bool attn_tcgen05_supported(const AttnParams& p) {
     return ready == cudaSuccess;
 }
 
-cudaError_t launch_attn_tcgen05(const AttnParams& p, int* status, cudaStream_t stream) {
+cudaError_t launch_attn_tcgen05(const AttnParams& p, int* status, cudaStream_t stream, bool stall) {
     switch (p.D) {
-        case 64: return launch_impl<64>(p, status, stream);
-        case 96: return launch_impl<96>(p, status, stream);
-        case 128: return launch_impl<128>(p, status, stream);
+        case 64: return launch_impl<64>(p, status, stream, stall);
+        case 96: return launch_impl<96>(p, status, stream, stall);
+        case 128: return launch_impl<128>(p, status, stream, stall);
         default: return cudaErrorInvalidValue;
     }
 }

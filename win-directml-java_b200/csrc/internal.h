@@ -107,7 +107,9 @@ constexpr int kStatusBufferInts = 8;
 // tcgen05 / TMEM / TMA kernel (fp16 operands, head_dim 64, 96, 128); status bit 3 = bounded wait ran out.
 // `status` is the context's status buffer (kStatusBufferInts ints).
 bool attn_tcgen05_supported(const AttnParams& p);
-cudaError_t launch_attn_tcgen05(const AttnParams& p, int* status, cudaStream_t stream);
+// stall (test hook): CTA 0 leaves one K/V copy of its first work item unissued, so a
+// bounded wait runs out (status bit 3).
+cudaError_t launch_attn_tcgen05(const AttnParams& p, int* status, cudaStream_t stream, bool stall = false);
 bool attn_tc_supported(const AttnParams& p);
 cudaError_t launch_attn_tc(const AttnParams& p, cudaStream_t stream);
 
