@@ -53,6 +53,14 @@ def test_prefill_bf16_output_within_tolerance_plus_rounding(ctx):
     assert np.all(np.abs(got - want) <= 2e-3 + half_ulp)
 
 
+def test_prefill_head_dim_256_tensor_cores(ctx):
+    """head_dim 256 (Gemma-3): one 128-row query tile per work item on the tcgen05 kernel, causal GQA over
+    several key tiles with a ragged last one."""
+    got, want = _prefill_case(ctx, B=2, S=520, Hq=8, Hkv=2, D=256, dtype=oracle.F16, out_dtype=oracle.F32,
+                              theta=1e4, seed=21)
+    assert_close(got, want, what="fp16 prefill D=256")
+
+
 @pytest.mark.parametrize("D", [32, 64, 128])
 def test_prefill_fp16_gqa_window(ctx, D):
     got, want = _prefill_case(ctx, B=2, S=200, Hq=8, Hkv=2, D=D, dtype=oracle.F16, out_dtype=oracle.F32,
@@ -214,6 +222,8 @@ def test_encoder_bf16_inputs(ctx, layout):
     (oracle.BF16, 0, 1e6, 96, 256),     # global layer
     (oracle.F16, 40, 1e4, 130, 128),    # a tensor-core head dim, ragged last tile
     (oracle.F32, 0, 1e6, 48, 256),      # fp32 end to end
+    (oracle.BF16, 512, 1e4, 700, 256),  # local layer over several 128-row tiles (tensor cores, one tile per item)
+    (oracle.F16, 0, 1e6, 600, 256),     # global layer, fp16
 ])
 def test_prefill_gemma_batched_matches_oracle(ctx, dtype, window, theta, S, D):
     """b2a_prefill_gemma: QK-norm (zero-centred RMSNorm, (1 + w)) and applyRopeHalf of every

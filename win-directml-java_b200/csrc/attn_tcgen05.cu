@@ -22,7 +22,9 @@
 // warpgroups, which keep a whole score row (128 fp32) in registers.
 // TMEM (512 columns): S_A 0..127, S_B 128..255 (fp32 scores; the softmax
 // writes P as fp16 pairs over the first 64 columns, and the PV MMA reads it
-// from TMEM), O_A at 256, O_B at 384.
+// from TMEM), O_A at 256, O_B at 384.  At head dim 256 a work item is one
+// query tile (S_A 0..127, O_A 128..383; warps 4-7 have no tile) and the K/V
+// ring has one stage (Q 64 KB + K 64 KB + V 64 KB of shared memory).
 // Softmax per tile: one TMEM read of the score row, row max (3-input max),
 // exp2 + row sum + P (f32x2 FMA/add); masks only on tiles that touch the
 // causal diagonal, the window start or the key end (a per-row visible key
@@ -60,11 +62,15 @@ constexpr int kThreadsTc = 384;
 // kRegsLaunch per thread (ptxas' limit for 384 threads and one CTA per SM, which
 // the host checks before launching); the control warpgroup returns registers so
 // the two softmax warpgroups can keep a whole 128-column score row resident.
-// 2 * kRegsSoftmax + kRegsControl == 3 * kRegsLaunch: the pool is used exactly.
+// 2 * kSoftmax + kControl == 3 * kRegsLaunch: the pool is used exactly.  At D = 256
+// the MMA issuer (16 QK and 8 PV MMAs per step) needs more of the control share.
 constexpr int kRegsLaunch = 168;
-constexpr int kRegsSoftmax = 216;
-constexpr int kRegsControl = 72;
-static_assert(2 * kRegsSoftmax + kRegsControl == 3 * kRegsLaunch, "register split must equal the launch pool");
+template <int D>
+struct RegSplit {
+    static constexpr int kSoftmax = D <= 128 ? 216 : 208;
+    static constexpr int kControl = 3 * kRegsLaunch - 2 * kSoftmax;
+    static_assert(kControl % 8 == 0 && kSoftmax % 8 == 0, "setmaxnreg takes multiples of 8");
+};
 constexpr uint64_t kWaitNs = 1000000000ull;  // 1 s
 constexpr float kRescaleThreshold = 8.0f;
 #ifndef B2A_POLY_PAIRS
@@ -95,9 +101,13 @@ struct TcGeo {
     static constexpr int NP = (D + 63) / 64;      // 128-byte panels per row
     static constexpr int kPanelBytes = 128 * 128;  // 128 rows x 128 B
     static constexpr int kTileBytes = NP * kPanelBytes;
-    static constexpr int kStages = D <= 64 ? 3 : 2;
-    static constexpr int oQ = 0;                   // Q_A, Q_B
-    static constexpr int oK = 2 * kTileBytes;
+    // query tiles per work item: TMEM holds kTiles x (S 128 + O D) columns, two tiles up to D = 128
+    static constexpr int kTiles = D <= 128 ? 2 : 1;
+    static constexpr uint32_t kOcol = 128u * kTiles;  // first O column (the S tiles come first)
+    // ring stages; at D = 256 one (a step's softmax + 24 MMAs outlast the next tiles' loads)
+    static constexpr int kStages = D <= 64 ? 3 : (D <= 128 ? 2 : 1);
+    static constexpr int oQ = 0;                   // Q_A (, Q_B)
+    static constexpr int oK = kTiles * kTileBytes;
     static constexpr int oV = oK + kStages * kTileBytes;
     static constexpr int oBar = oV + kStages * kTileBytes;
     static constexpr int kBytes = oBar + 512;  // barriers, TMEM address, abort flag, work-item mailbox
@@ -340,9 +350,10 @@ __device__ __forceinline__ void store8(void* out, int64_t off, const float* v, i
 // ---------------------------------------------------------------- kernel
 // kAdditive: the additive [B][S] key mask is applied (its own instantiation, so the
 // mask loads do not weigh on the register budget of the unmasked kernels).
-// A work item is the pair of query tiles (A, B) starting at row 2 * 128 * pair of one
-// (batch, head).  Items are numbered pair-fastest, longest causal pair first within a
-// head: w = x + n_pairs * (h + Hq * b), pair = n_pairs - 1 - x when causal.  CTAs take
+// A work item is the group of `tiles` query tiles (A, B; one tile, A, when the head dim
+// leaves TMEM room for one) starting at row 128 * tiles * pair of one (batch, head).
+// Items are numbered pair-fastest, longest causal pair first within a head:
+// w = x + n_pairs * (h + Hq * b), pair = n_pairs - 1 - x when causal.  CTAs take
 // items in that order from a device counter, so the heads in flight at any time are a
 // few consecutive ones (their K/V stay in L2) and the longest items start first.
 struct ItemGeo {
@@ -356,15 +367,15 @@ struct ItemGeo {
     bool uniform;     // no valid key (key_len <= 0): every key weighs the same
 };
 
-__device__ __forceinline__ ItemGeo item_geo(int w, int n_pairs, int Hq, int S, int causal, int window,
+__device__ __forceinline__ ItemGeo item_geo(int w, int n_pairs, int tiles, int Hq, int S, int causal, int window,
                                             const int32_t* key_len) {
     ItemGeo g;
     const int x = w % n_pairs, rest = w / n_pairs;
     g.h = rest % Hq;
     g.b = rest / Hq;
     const int pair = causal ? n_pairs - 1 - x : x;
-    g.q0a = pair * 2 * kBM;
-    g.q0b = g.q0a + kBM;
+    g.q0a = pair * tiles * kBM;
+    g.q0b = tiles == 2 ? g.q0a + kBM : S;  // a single-tile item's tile B lies past the sequence
     g.kb0 = g.kb1 = 0;
     g.ke0 = g.ke1 = S;
     g.uniform = false;
@@ -505,14 +516,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const uint32_t tmem = *tmem_holder;
 
     if (warp >= 8) {
-      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(RegSplit<D>::kControl));
       if (warp == 8) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             const int S = p.S, causal = p.causal, window = p.window, Hq = p.Hq, G = p.G;
             const int32_t* const key_len = p.key_len;
             int* const sched = p.sched;
-            const int n_pairs = (S + 2 * kBM - 1) / (2 * kBM);
+            const int n_pairs = (S + Gm::kTiles * kBM - 1) / (Gm::kTiles * kBM);
             int k = 0;        // work items published
             int g = 0;        // ring items issued
             int q_items = 0;  // work items whose Q tiles were issued
@@ -522,13 +533,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 // slot k % 2 is free once every reader of item k-2 is done with it
                 if (k >= 2 && !mbar_wait(bItemEmpty(slot), ((k >> 1) - 1) & 1, abort_flag, status)) break;
                 const int w = atomicAdd(sched, 1);
-                const ItemGeo it = item_geo(w < n_items ? w : 0, n_pairs, Hq, S, causal, window, key_len);
+                const ItemGeo it = item_geo(w < n_items ? w : 0, n_pairs, Gm::kTiles, Hq, S, causal, window, key_len);
                 publish_item(slots + kSlotInts * slot, w < n_items, it, causal, window);
                 mbar_arrive(bItemFull(slot));  // release: the slot's values are visible to the waiters
                 if (w >= n_items) break;
                 const int kvh = it.h / G;
                 bool ok = true;
-                for (int t = 0; t < 2 && ok; ++t) {
+                for (int t = 0; t < Gm::kTiles && ok; ++t) {
                     if (k >= 1 && !mbar_wait(bQempty(t), (k - 1) & 1, abort_flag, status)) {
                         ok = false;
                         break;
@@ -568,7 +579,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             }
             // every copy this thread issued lands before the CTA may exit
             if (q_items > 0)
-                for (int t = 0; t < 2; ++t) mbar_drain(bQfull(t), (q_items - 1) & 1);
+                for (int t = 0; t < Gm::kTiles; ++t) mbar_drain(bQfull(t), (q_items - 1) & 1);
             for (int i = (g > ST ? g - ST : 0); i < g; ++i)
                 if (i != skip_g) mbar_drain(bKVfull(i % ST), (i / ST) & 1);
         }
@@ -616,7 +627,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             // 64-column panels kPanelBytes apart (LBO)
             auto issue_pv = [&](int t, int st, uint32_t acc) {
                 const uint32_t b0 = v_lo + (uint32_t)(st * Gm::kTileBytes >> 4);
-                const uint32_t d = tmem + 256u + 128u * t, a = tmem + 128u * t;
+                const uint32_t d = tmem + Gm::kOcol + 128u * t, a = tmem + 128u * t;
                 umma_ts_w<-1>(ln, d, a, b0, v_hi, idp, acc);
 #pragma unroll
                 for (int kk = 1; kk < kBN / 16; ++kk) umma_ts_w<1>(ln, d, a + kk * 8u, b0 + kk * 128u, v_hi, idp);
@@ -631,14 +642,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 if (!ms[kSlotValid]) break;
                 const int nt0 = ms[kSlotNt0], nt1 = ms[kSlotNt1], n_max = max(nt0, nt1);
                 ok = __all_sync(0xffffffffu, mbar_wait(bQfull(0), k & 1, abort_flag, status) &&
-                                                 mbar_wait(bQfull(1), k & 1, abort_flag, status));
+                                                 (Gm::kTiles == 1 || mbar_wait(bQfull(1), k & 1, abort_flag, status)));
                 if (ok) ok = wait_item(g);
                 if (!ok) break;
                 // S_t(0); a tile with at most one key tile reads Q_t for the last time here
                 if (nt0 > 0) issue_qk(0, g % ST);
                 if (nt0 <= 1) umma_commit_w(ln, bQempty(0));
                 if (nt1 > 0) issue_qk(1, g % ST);
-                if (nt1 <= 1) umma_commit_w(ln, bQempty(1));
+                if (Gm::kTiles == 2 && nt1 <= 1) umma_commit_w(ln, bQempty(1));
                 umma_commit_w(ln, bKVempty(g % ST));  // ring item 0 (K(0)) read by both tiles
                 for (int j = 0; j < n_max && ok; ++j) {
                     const int st = (g + j + 1) % ST;  // ring item j+1: V(j), K(j+1)
@@ -682,13 +693,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         }
       }
     } else {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(RegSplit<D>::kSoftmax));
         // ------------------------------------------------------------ softmax groups
         const int t = warp >> 2;       // 0: tile A, 1: tile B
         const int row = tid & 127;     // TMEM lane within the group
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const uint32_t s_addr = lane_base + (t ? 128u : 0u);
-        const uint32_t o_addr = lane_base + (t ? 384u : 256u);
+        const uint32_t o_addr = lane_base + Gm::kOcol + (t ? 128u : 0u);
         const int S = p.S, causal = p.causal, window = p.window;
         const float* const mask = kAdditive ? p.mask : nullptr;
         const float scale = p.scale;
@@ -934,7 +945,10 @@ cudaError_t kernel_ready_for(const AttnParams& p) {
 }
 
 // query-tile pairs x heads x batch
-int64_t work_items(const AttnParams& a) { return (int64_t)((a.S + 2 * kBM - 1) / (2 * kBM)) * a.Hq * a.B; }
+int64_t work_items(const AttnParams& a) {
+    const int rows = (a.D <= 128 ? 2 : 1) * kBM;  // TcGeo<D>::kTiles query tiles per item
+    return (int64_t)((a.S + rows - 1) / rows) * a.Hq * a.B;
+}
 
 template <int D>
 cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream, bool stall) {
@@ -988,7 +1002,7 @@ cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream, b
 bool attn_tcgen05_supported(const AttnParams& p) {
     // fp16 operands only: P goes to TMEM as fp16 and both MMA operands share one type
     if (p.in_dtype != kF16) return false;
-    if (!(p.D == 64 || p.D == 96 || p.D == 128)) return false;
+    if (!(p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256)) return false;
     const int64_t strides[] = {p.q_sb, p.q_ss, p.q_sh, p.k_sb, p.k_ss, p.k_sh};
     for (int64_t s : strides)
         if (s % 8 != 0 || s <= 0) return false;
@@ -998,7 +1012,8 @@ bool attn_tcgen05_supported(const AttnParams& p) {
     // the work-item counter reaches items + grid within int32
     if (p.Hq > 65535 || p.B > 65535 || work_items(p) > INT32_MAX / 2 || encode_fn() == nullptr) return false;
     const cudaError_t ready = p.D == 64 ? kernel_ready_for<64>(p) : p.D == 96 ? kernel_ready_for<96>(p)
-                                                                               : kernel_ready_for<128>(p);
+                                                                               : p.D == 128 ? kernel_ready_for<128>(p)
+                                                                                            : kernel_ready_for<256>(p);
     return ready == cudaSuccess;
 }
 
@@ -1007,6 +1022,7 @@ cudaError_t launch_attn_tcgen05(const AttnParams& p, int* status, cudaStream_t s
         case 64: return launch_impl<64>(p, status, stream, stall);
         case 96: return launch_impl<96>(p, status, stream, stall);
         case 128: return launch_impl<128>(p, status, stream, stall);
+        case 256: return launch_impl<256>(p, status, stream, stall);
         default: return cudaErrorInvalidValue;
     }
 }
