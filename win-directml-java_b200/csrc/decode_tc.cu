@@ -138,7 +138,8 @@ __device__ __forceinline__ void head_load(HeadLoad<D>& h, const void* src, int64
 // warp-private.
 template <int D>
 __device__ __forceinline__ void prep_finish(const DecodeParams& p, const HeadLoad<D>& h, int dtype, bool has_bias,
-                                            const float* norm_w, bool rope, const double* cs, float* vec, int lane) {
+                                            bool has_norm, const float (&norm_w)[D / 32], bool rope, const double* cs,
+                                            float* vec, int lane) {
     double ss = 0.0;
     float x[D / 32];
 #pragma unroll
@@ -147,16 +148,14 @@ __device__ __forceinline__ void prep_finish(const DecodeParams& p, const HeadLoa
         if (has_bias) x[j] = __fadd_rn(x[j], h.bias[j]);  // projection bias, fp32
         ss += (double)x[j] * (double)x[j];
     }
-    if (norm_w != nullptr) {
+    if (has_norm) {
         // Gemma3ReferenceMath.rmsNormZeroCentered: double sum of squares,
         // float rms, (float)(x*rms * (1 + w)) (INF/gemma/Gemma3ReferenceMath.java:32-40).
         ss = warp_sum_d(ss);
         const float rms = (float)(1.0 / sqrt(__dadd_rn(ss / (double)D, (double)p.norm_eps)));
 #pragma unroll
-        for (int j = 0; j < D / 32; ++j) {
-            const int d = lane + 32 * j;
-            x[j] = (float)__dmul_rn((double)__fmul_rn(x[j], rms), __dadd_rn(1.0, (double)norm_w[d]));
-        }
+        for (int j = 0; j < D / 32; ++j)
+            x[j] = (float)__dmul_rn((double)__fmul_rn(x[j], rms), __dadd_rn(1.0, (double)norm_w[j]));
     }
 #pragma unroll
     for (int j = 0; j < D / 32; ++j) vec[lane + 32 * j] = x[j];
@@ -356,6 +355,15 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
                 head_load<D>(qload[i], p.q, (int64_t)b * q_stride_of(p) + (int64_t)(h0 + hl) * D, p.q_dtype,
                              p.q_bias ? p.q_bias + (h0 + hl) * D : nullptr, lane);
         }
+        // QK-norm weights, elements lane + 32 j: the q weights serve every q head of the warp
+        float qnw[D / 32], knw[D / 32];
+        const float* const qn = p.append ? p.q_norm_w : nullptr;
+        const float* const kn = (has_new && warp == 0) ? p.k_norm_w : nullptr;
+#pragma unroll
+        for (int j = 0; j < D / 32; ++j) {
+            qnw[j] = qn != nullptr ? __ldg(qn + lane + 32 * j) : 0.f;
+            knw[j] = kn != nullptr ? __ldg(kn + lane + 32 * j) : 0.f;
+        }
         HeadLoad<D> nload;  // warp 0: the new key row, warp 1: the new value row
         if (has_new && warp < 2)
             head_load<D>(nload, warp == 0 ? p.k_new : p.v_new, (int64_t)b * kvn_stride_of(p) + (int64_t)kvh * D,
@@ -385,8 +393,7 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
                 for (int d = lane; d < D; d += 32) qrow[d] = qlo[d] = Elem<T>::from_float(0.f);
                 continue;
             }
-            prep_finish<D>(p, qload[i], p.q_dtype, p.q_bias != nullptr, p.append ? p.q_norm_w : nullptr, rope, cs_s,
-                           vec, lane);
+            prep_finish<D>(p, qload[i], p.q_dtype, p.q_bias != nullptr, qn != nullptr, qnw, rope, cs_s, vec, lane);
             for (int d = lane; d < D; d += 32) {
                 const T hi = Elem<T>::from_float(vec[d]);
                 qrow[d] = hi;
@@ -396,7 +403,7 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         }
         if (has_new) {
             if (warp == 0) {
-                prep_finish<D>(p, nload, p.q_dtype, p.k_bias != nullptr, p.k_norm_w, rope, cs_s, vec, lane);
+                prep_finish<D>(p, nload, p.q_dtype, p.k_bias != nullptr, kn != nullptr, knw, rope, cs_s, vec, lane);
                 T* dst = static_cast<T*>(p.k_cache) + b * p.stride_b + kvh * p.stride_h + (int64_t)L * p.stride_pos;
                 for (int d = lane; d < D; d += 32) {
                     const T v = Elem<T>::from_float(vec[d]);
