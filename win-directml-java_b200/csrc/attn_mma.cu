@@ -10,6 +10,7 @@
 // The semantics are the same as attn_simt.cu; see there for citations.
 #include <math.h>
 
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -241,14 +242,19 @@ __global__ void __launch_bounds__(kThreads) attn_mma_kernel(const __grid_constan
 
 template <int D, typename T>
 cudaError_t launch_impl(const AttnParams& p, cudaStream_t stream) {
-    static bool configured = false;
+    // the dynamic shared-memory size is a per-device kernel attribute: set once per device
+    constexpr int kMaxDevices = 64;
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t err[kMaxDevices];
     const size_t smem = AGeo<D>::kTotal;
-    if (!configured) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::call_once(once[dev], [dev, smem] {
         cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<D, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)smem);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+        err[dev] = e;
+    });
+    if (err[dev] != cudaSuccess) return err[dev];
     dim3 grid((p.S + kBM - 1) / kBM, p.Hq, p.B);
     attn_mma_kernel<D, T><<<grid, kThreads, smem, stream>>>(p);
     return cudaGetLastError();

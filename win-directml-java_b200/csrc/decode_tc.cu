@@ -657,22 +657,29 @@ struct LaunchInfo {
     size_t smem = 0;
 };
 
+// Kernel attributes are per device: set up once for each device (the caller has made
+// `device` current).
 template <int D, typename T>
 LaunchInfo launch_info(int device) {
-    static std::once_flag once;
-    static LaunchInfo info;
-    static cudaError_t err = cudaSuccess;
-    std::call_once(once, [&] {
+    constexpr int kMaxDevices = 64;
+    static std::once_flag once[kMaxDevices];
+    static LaunchInfo info[kMaxDevices];
+    static cudaError_t err[kMaxDevices];
+    if (device < 0 || device >= kMaxDevices) return LaunchInfo{};
+    std::call_once(once[device], [device] {
         auto kern = decode_tc_kernel<D, T>;
-        info.smem = Geo<D>::kTotal;
-        err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)info.smem);
+        LaunchInfo li;
+        li.smem = Geo<D>::kTotal;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)li.smem);
         int occ = 0, sms = 0;
-        if (err == cudaSuccess) err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, info.smem);
-        if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-        info.grid = occ * sms;
+        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, li.smem);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        li.grid = occ * sms;
+        info[device] = li;
+        err[device] = e;
     });
-    if (err != cudaSuccess) return LaunchInfo{};
-    return info;
+    if (err[device] != cudaSuccess) return LaunchInfo{};
+    return info[device];
 }
 
 template <typename F>
