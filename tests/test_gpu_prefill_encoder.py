@@ -260,3 +260,35 @@ def test_prefill_gemma_batched_matches_oracle(ctx, dtype, window, theta, S, D):
     want_k = oracle.round_to(k_r, dtype)
     ulp = {oracle.F16: 2.0 ** -10, oracle.BF16: 2.0 ** -7, oracle.F32: 2.0 ** -23}[dtype]
     assert np.all(np.abs(to_np(kr) - want_k) <= ulp * np.maximum(np.abs(want_k), 2.0 ** -14))
+
+
+def test_generic_kernel_key_split_back_to_back(ctx):
+    """fp32 launches too small to fill the GPU split each query block's keys over several CTAs and merge
+    the chunks; launches of different shapes run back to back without a synchronisation in between, so a
+    per-block counter left non-zero, or a merge reading another launch's slots, would show here."""
+    import torch
+    import b200attn
+    cases = []
+    for i, (S, Hq, Hkv, D, window) in enumerate([(300, 6, 2, 48, 100), (256, 9, 3, 64, 0), (130, 2, 2, 40, 0)]):
+        q = normal(700 + i, (1, S, Hq, D), oracle.F32)
+        k = normal(710 + i, (1, S, Hkv, D), oracle.F32)
+        v = normal(720 + i, (1, S, Hkv, D), oracle.F32)
+        scale = float(np.float32(1.0 / math.sqrt(D)))
+        want = oracle.prefill(q, k, v, B=1, S=S, Hq=Hq, Hkv=Hkv, D=D, scale=scale, rope_theta=1e4, window=window)
+        o = torch.full((1, S, Hq, D), float("nan"), dtype=torch.float32, device="cuda")
+        b200attn.prefill_causal(ctx, to_dev(q, oracle.F32), to_dev(k, oracle.F32), to_dev(v, oracle.F32), o, scale,
+                                rope_mode=b200attn.ROPE_NEOX, rope_theta=1e4, window=window)
+        cases.append((o, want, f"fp32 prefill S={S} D={D} window={window}"))
+    lens = [200, 17, 1]
+    shape = (3, 4, 200, 64)  # head-major encoder, fp32, key padding
+    q, k, v = (normal(730 + j, shape, oracle.F32) for j in range(3))
+    want = oracle.encoder_minilm(q, k, v, lens, B=3, H=4, S=200, D=64, layout=0)
+    y = torch.full(shape, float("nan"), dtype=torch.float32, device="cuda")
+    b200attn.mha(ctx, to_dev(q, oracle.F32), to_dev(k, oracle.F32), to_dev(v, oracle.F32), y, 1.0 / 8.0,
+                 key_lengths=torch.from_numpy(np.asarray(lens, np.int32)).cuda(), layout=b200attn.HEAD_MAJOR)
+    cases.append((y, want, "fp32 encoder, key lengths"))
+    torch.cuda.synchronize()
+    ctx.check_device_status()
+    for got, want, what in cases:
+        err, _ = assert_close(to_np(got), want, what=what)
+        assert err < 1e-4, what  # fp32 end to end

@@ -32,6 +32,10 @@ struct b2a_context {
     // prefill workspace: rope table + rotated q/k staging
     void* pf_ws = nullptr;
     size_t pf_ws_bytes = 0;
+    // generic-kernel key split: [counters][partial slots]; counters zero between launches
+    void* split_ws = nullptr;
+    size_t split_ws_bytes = 0;
+    size_t split_counter_ints = 0;
     // test hook (b2a_test_inject_wait_timeout): the next tcgen05 attention launch
     // leaves one K/V copy unissued
     bool inject_wait_timeout = false;
@@ -76,7 +80,7 @@ size_t dtype_size(int d) { return d == B2A_FLOAT32 ? 4 : 2; }
 
 int ensure_buffer(b2a_context* ctx, void** buf, size_t* have, size_t need, const char* what) {
     if (*have >= need) return B2A_OK;
-    const size_t other = (buf == &ctx->dec_ws ? ctx->pf_ws_bytes : ctx->dec_ws_bytes);
+    const size_t other = ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes - *have;
     if (ctx->ws_limit != 0 && need + other > ctx->ws_limit)
         return fail(ctx, B2A_EOOM, "%s workspace of %zu bytes exceeds the context limit of %zu bytes", what,
                     need + other, ctx->ws_limit);
@@ -125,6 +129,26 @@ cudaError_t launch_attention(b2a_context* ctx, const AttnParams& p, cudaStream_t
         return launch_attn_tcgen05(p, ctx->status, s, stall);
     }
     if (attn_tc_supported(p)) return launch_attn_tc(p, s);
+    // generic kernel: launches too small to fill the GPU split each query block's keys
+    // over several CTAs; without room for the split workspace they run unsplit
+    size_t part_bytes = 0, counter_ints = 0;
+    const int nsplit = attn_simt_split_plan(p, ctx->sm_count, &part_bytes, &counter_ints);
+    if (nsplit > 1) {
+        const size_t counter_bytes = (counter_ints * sizeof(int) + 255) / 256 * 256;
+        const bool grow = counter_bytes + part_bytes > ctx->split_ws_bytes;
+        if (ensure_buffer(ctx, &ctx->split_ws, &ctx->split_ws_bytes, counter_bytes + part_bytes, "attention split") ==
+            B2A_OK) {
+            if (grow || counter_ints > ctx->split_counter_ints) {
+                const cudaError_t e = cudaMemsetAsync(ctx->split_ws, 0, counter_bytes, s);
+                if (e != cudaSuccess) return e;
+                ctx->split_counter_ints = counter_bytes / sizeof(int);
+            }
+            const SimtSplit sp{reinterpret_cast<float*>(static_cast<char*>(ctx->split_ws) + counter_bytes),
+                               static_cast<int*>(ctx->split_ws), nsplit, kSimtSplitKeys};
+            return launch_attn_simt(p, s, &sp);
+        }
+        ctx->last_error.clear();  // the refused workspace is not an error of this call
+    }
     return launch_attn_simt(p, s);
 }
 
@@ -248,6 +272,7 @@ B2A_API int b2a_destroy(b2a_context* ctx) {
         if (ctx->status) cudaFree(ctx->status);
         if (ctx->dec_ws) cudaFree(ctx->dec_ws);
         if (ctx->pf_ws) cudaFree(ctx->pf_ws);
+        if (ctx->split_ws) cudaFree(ctx->split_ws);
     }
     delete ctx;
     return B2A_OK;
@@ -271,7 +296,7 @@ B2A_API int b2a_set_workspace_limit(b2a_context* ctx, size_t bytes) {
 
 B2A_API int b2a_workspace_bytes(const b2a_context* ctx, size_t* bytes) {
     if (!ctx || !bytes) return B2A_EINVAL;
-    *bytes = ctx->dec_ws_bytes + ctx->pf_ws_bytes;
+    *bytes = ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes;
     return B2A_OK;
 }
 

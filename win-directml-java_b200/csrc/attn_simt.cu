@@ -20,6 +20,11 @@
 // multiples of 4 elements) each thread owns fixed 4-element groups of a tile and
 // loads the next tile's groups into registers while the current tile is used, so a
 // CTA's sequential key tiles do not each wait for a global load.
+// Key split (launches too small to fill the GPU, e.g. one short causal prefill):
+// each query block's key range is cut into chunks of SimtSplit::split_keys keys, one
+// CTA per chunk; a chunk's CTA writes its rows' (max, sum, unnormalised O) to a slot,
+// and the last CTA of the block to finish (a per-block counter) combines the slots
+// (log-sum-exp) and resets the counter, so the counters are zero between launches.
 #include <math.h>
 
 #include <type_traits>
@@ -58,7 +63,8 @@ __device__ __forceinline__ void raw4_store(float* dst, uint4 r, int dtype) {
 }
 
 template <int kHT, int kNPL, bool kVec>
-__global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_constant__ AttnParams p, int G) {
+__global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_constant__ AttnParams p, int G,
+                                                               const SimtSplit split) {
     extern __shared__ float sm[];
     const int D = p.D, Dp = D + 1;
     float* ks = sm;                          // [kTileKeys][D + 1]
@@ -70,21 +76,15 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
     const float* const mask = p.mask;
     const int64_t k_ss = p.k_ss;
     const int S = p.S;
-    const int s0 = blockIdx.x * kRows;
+    const int nsplit = split.nsplit;
+    const int qblk = (int)blockIdx.x / nsplit, part = (int)blockIdx.x - qblk * nsplit;
+    const int s0 = qblk * kRows;
     const int chunks = (G + kHeads - 1) / kHeads;
     const int kvh = blockIdx.y / chunks, h0 = kvh * G + (blockIdx.y % chunks) * kHeads;
     const int nh = min(kHeads, kvh * G + G - h0);  // heads of this CTA
     const int b = blockIdx.z;
     const int s = s0 + warp;
     const bool row_valid = s < S;
-
-    // this row's query vectors, as fp32 (padding heads zero)
-    for (int g = 0; g < kHT; ++g)
-        for (int d = lane; d < D; d += 32)
-            qs[(warp * kHT + g) * D + d] =
-                row_valid && g < nh
-                    ? load_as_float(p.q, b * p.q_sb + (int64_t)s * p.q_ss + (int64_t)(h0 + g) * p.q_sh + d, p.in_dtype)
-                    : 0.f;
 
     // visible keys of this row, and the CTA's union of them
     int first = 0, last = S - 1;
@@ -103,6 +103,23 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
         cta_last = s_hi;
         cta_first = p.window > 0 ? max(0, s0 - p.window + 1) : 0;
     }
+    // key split: this CTA's chunk of the block's range (the block's chunk count from its whole range)
+    int n_parts = 1;
+    if (nsplit > 1) {
+        n_parts = min(nsplit, (cta_last - cta_first + split.split_keys) / split.split_keys);
+        if (part >= n_parts) return;  // past the block's keys (the whole CTA, before any barrier)
+        const int lo = cta_first + part * split.split_keys;
+        cta_last = min(cta_last, lo + split.split_keys - 1);
+        cta_first = lo;
+    }
+
+    // this row's query vectors, as fp32 (padding heads zero)
+    for (int g = 0; g < kHT; ++g)
+        for (int d = lane; d < D; d += 32)
+            qs[(warp * kHT + g) * D + d] =
+                row_valid && g < nh
+                    ? load_as_float(p.q, b * p.q_sb + (int64_t)s * p.q_ss + (int64_t)(h0 + g) * p.q_sh + d, p.in_dtype)
+                    : 0.f;
     const float sl2 = p.scale * kLog2e;
     float acc[kHT][kNPL];
     float m[kHT], l[kHT];
@@ -259,40 +276,123 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
         }
         __syncthreads();
     }
-    if (!row_valid) return;
+    if (n_parts == 1) {
+        if (!row_valid) return;
 #pragma unroll
-    for (int g = 0; g < kHT; ++g) {
-        if (g >= nh) break;
-        const float inv = 1.f / l[g];
-        const int64_t qo = b * p.q_sb + (int64_t)s * p.q_ss + (int64_t)(h0 + g) * p.q_sh;
+        for (int g = 0; g < kHT; ++g) {
+            if (g >= nh) break;
+            const float inv = 1.f / l[g];
+            const int64_t qo = b * p.q_sb + (int64_t)s * p.q_ss + (int64_t)(h0 + g) * p.q_sh;
 #pragma unroll
-        for (int i = 0; i < kNPL; ++i) {
-            const int d = lane + 32 * i;
-            if (d < D) store_from_float(p.o, qo + d, acc[g][i] * inv, p.out_dtype);
+            for (int i = 0; i < kNPL; ++i) {
+                const int d = lane + 32 * i;
+                if (d < D) store_from_float(p.o, qo + d, acc[g][i] * inv, p.out_dtype);
+            }
+        }
+        return;
+    }
+    // this chunk's partial state: per row and head, O (unnormalised) [D], max, sum
+    const int n_qblk = (int)gridDim.x / nsplit;
+    const int blk = ((int)blockIdx.z * (int)gridDim.y + (int)blockIdx.y) * n_qblk + qblk;
+    const int row_floats = D + 2;
+    auto slot_of = [&](int pt) { return split.part + ((size_t)blk * nsplit + pt) * (kRows * kHT * row_floats); };
+    if (row_valid) {
+        float* mine = slot_of(part);
+#pragma unroll
+        for (int g = 0; g < kHT; ++g) {
+            float* r = mine + (warp * kHT + g) * row_floats;
+#pragma unroll
+            for (int i = 0; i < kNPL; ++i) {
+                const int d = lane + 32 * i;
+                if (d < D) r[d] = acc[g][i];
+            }
+            if (lane == 0) {
+                r[D] = m[g];
+                r[D + 1] = l[g];
+            }
         }
     }
+    __threadfence();
+    __syncthreads();
+    __shared__ int is_last;
+    if (threadIdx.x == 0) is_last = atomicAdd(split.cnt + blk, 1) == n_parts - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    if (row_valid) {
+#pragma unroll
+        for (int g = 0; g < kHT; ++g) {
+            if (g >= nh) break;
+            const int off = (warp * kHT + g) * row_floats;
+            float M = -INFINITY;
+            for (int pt = 0; pt < n_parts; ++pt) M = fmaxf(M, __ldcg(slot_of(pt) + off + D));
+            const float base = M == -INFINITY ? 0.f : M;
+            float L = 0.f, o[kNPL];
+#pragma unroll
+            for (int i = 0; i < kNPL; ++i) o[i] = 0.f;
+            for (int pt = 0; pt < n_parts; ++pt) {
+                const float* r = slot_of(pt) + off;
+                const float f = fast_exp2(__ldcg(r + D) - base);  // 0 for a chunk with none of the row's keys
+                L += f * __ldcg(r + D + 1);
+#pragma unroll
+                for (int i = 0; i < kNPL; ++i) {
+                    const int d = lane + 32 * i;
+                    if (d < D) o[i] += f * __ldcg(r + d);
+                }
+            }
+            const float inv = 1.f / L;
+            const int64_t qo = b * p.q_sb + (int64_t)s * p.q_ss + (int64_t)(h0 + g) * p.q_sh;
+#pragma unroll
+            for (int i = 0; i < kNPL; ++i) {
+                const int d = lane + 32 * i;
+                if (d < D) store_from_float(p.o, qo + d, o[i] * inv, p.out_dtype);
+            }
+        }
+    }
+    if (threadIdx.x == 0) split.cnt[blk] = 0;  // zero again for the next launch
 }
 
 }  // namespace
 
-cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t stream) {
+namespace {
+int head_tile(const AttnParams& p) {
+    const int G = p.Hq / p.Hkv;
+    const int heads = G < kHeads ? G : kHeads;
+    return heads <= 1 ? 1 : heads <= 2 ? 2 : heads <= 4 ? 4 : 8;
+}
+}  // namespace
+
+int attn_simt_split_plan(const AttnParams& p, int sm_count, size_t* part_bytes, size_t* counter_ints) {
+    *part_bytes = 0;
+    *counter_ints = 0;
+    const int G = p.Hq / p.Hkv;
+    const int64_t blocks = (int64_t)((p.S + kRows - 1) / kRows) * p.Hkv * ((G + kHeads - 1) / kHeads) * p.B;
+    // split only launches that leave SMs idle, into as many chunks as the longest range has
+    const int nsplit = (p.S + kSimtSplitKeys - 1) / kSimtSplitKeys;
+    if (blocks >= 2 * (int64_t)sm_count || nsplit <= 1 || blocks * nsplit > 65535) return 1;
+    *part_bytes = (size_t)blocks * nsplit * kRows * head_tile(p) * (p.D + 2) * sizeof(float);
+    *counter_ints = (size_t)blocks;
+    return nsplit;
+}
+
+cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t stream, const SimtSplit* split) {
     const int G = p.Hq / p.Hkv;
     const int chunks = (G + kHeads - 1) / kHeads;
-    const int heads = G < kHeads ? G : kHeads;
-    const int ht = heads <= 1 ? 1 : heads <= 2 ? 2 : heads <= 4 ? 4 : 8;
+    const int ht = head_tile(p);
+    const SimtSplit sp = split != nullptr ? *split : SimtSplit{nullptr, nullptr, 1, kSimtSplitKeys};
     const size_t smem =
         ((size_t)2 * kTileKeys * (p.D + 1) + (size_t)kRows * ht * p.D + (size_t)kRows * kTileKeys * ht) * sizeof(float);
     // 4-element groups: head dim, strides and bases in whole groups (16 B for fp32, 8 B for 16-bit)
     const size_t es = p.in_dtype == kF32 ? 4 : 2;
     const bool vec = p.D % 4 == 0 && p.k_ss % 4 == 0 && p.k_sh % 4 == 0 && p.k_sb % 4 == 0 &&
                      (uintptr_t)p.k % (4 * es) == 0 && (uintptr_t)p.v % (4 * es) == 0;
-    const dim3 grid((p.S + kRows - 1) / kRows, p.Hkv * chunks, p.B);
+    const dim3 grid((p.S + kRows - 1) / kRows * sp.nsplit, p.Hkv * chunks, p.B);
     auto go = [&](auto kernel) {
         if (smem > 48 * 1024) {
             const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (e != cudaSuccess) return e;
         }
-        kernel<<<grid, kRows * 32, smem, stream>>>(p, G);
+        kernel<<<grid, kRows * 32, smem, stream>>>(p, G, sp);
         return cudaGetLastError();
     };
     const int npl = (p.D + 31) / 32;

@@ -95,7 +95,18 @@ struct AttnParams {
     float scale;
 };
 
-cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t stream);
+// Key split of the generic kernel: partial slots and per-query-block counters (zero
+// between launches) in a caller-provided workspace; nsplit == 1 means no split.
+constexpr int kSimtSplitKeys = 64;
+struct SimtSplit {
+    float* part;
+    int* cnt;
+    int nsplit;
+    int split_keys;
+};
+// Chunks per query block for this launch (1: no split) and the workspace it needs.
+int attn_simt_split_plan(const AttnParams& p, int sm_count, size_t* part_bytes, size_t* counter_ints);
+cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t stream, const SimtSplit* split = nullptr);
 // The context's device status buffer: words [0, kStatusWords) are the error flags
 // b2a_check_device_status reports and clears; words kStatusSchedWord and the next one are
 // the persistent prefill kernel's work-item counters (zero between launches: the last CTA
