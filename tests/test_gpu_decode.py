@@ -79,6 +79,15 @@ def test_decode_gemma_shape_local_and_global(ctx, window, theta):
               rope_mode="gemma", theta=theta, window=window, qk_norm=True, seed=31)
 
 
+def test_decode_batch_sizes_shrinking_and_growing_on_one_context(ctx):
+    """The workspace's merge counters must stay zero between calls whatever the batch order: a large batch,
+    then a small one whose partial slots must not land where a larger batch keeps counters, then a medium
+    one, all with contexts long enough that units are split across CTAs and merged."""
+    rng = np.random.default_rng(11)
+    for i, B in enumerate([160, 4, 64]):
+        _run_case(ctx, B=B, Hq=4, Hkv=2, D=64, max_seq=2048, lens=rng.integers(1000, 2047, B), seed=120 + i)
+
+
 def test_decode_pos_major_multi_kv_head(ctx):
     _run_case(ctx, B=3, Hq=8, Hkv=2, D=128, max_seq=400, lens=[10, 399, 200], layout=oracle.KV_POS_MAJOR, seed=41)
 

@@ -28,14 +28,17 @@ struct b2a_context {
     // decode workspace: [counters][partials]
     void* dec_ws = nullptr;
     size_t dec_ws_bytes = 0;
-    size_t dec_counter_ints = 0;
+    // counter region at the start of dec_ws, partial slots after it; the region never
+    // shrinks (a later, smaller batch's slots would otherwise land on counters a larger
+    // batch relies on being zero) and is zeroed whenever it grows or the buffer is new
+    size_t dec_counter_bytes = 0;
     // prefill workspace: rope table + rotated q/k staging
     void* pf_ws = nullptr;
     size_t pf_ws_bytes = 0;
-    // generic-kernel key split: [counters][partial slots]; counters zero between launches
+    // generic-kernel key split: [counters][partial slots], the same layout rules as dec_ws
     void* split_ws = nullptr;
     size_t split_ws_bytes = 0;
-    size_t split_counter_ints = 0;
+    size_t split_counter_bytes = 0;
     // test hook (b2a_test_inject_wait_timeout): the next tcgen05 attention launch
     // leaves one K/V copy unissued
     bool inject_wait_timeout = false;
@@ -98,6 +101,27 @@ int ensure_buffer(b2a_context* ctx, void** buf, size_t* have, size_t need, const
     return B2A_OK;
 }
 
+// Sizes a [counters][partial slots] workspace: the counter region keeps the largest size
+// any call needed, the partial slots start after it, and the counters are zeroed (on
+// `stream`, or synchronously when it is null and `sync`) when the buffer is new or the
+// region grows.  Returns the counter region's size in *counter_bytes.
+int ensure_counted_buffer(b2a_context* ctx, void** buf, size_t* have, size_t* region, size_t counter_ints,
+                          size_t partial_bytes, const char* what, cudaStream_t stream, bool sync,
+                          size_t* counter_bytes) {
+    const size_t need_counters = (counter_ints * sizeof(int) + 255) / 256 * 256;
+    const size_t cb = std::max(need_counters, *region);
+    const bool grow = cb + partial_bytes > *have;
+    const int rc = ensure_buffer(ctx, buf, have, cb + partial_bytes, what);
+    if (rc != B2A_OK) return rc;
+    if (grow || cb > *region) {
+        const cudaError_t e = sync ? cudaMemset(*buf, 0, cb) : cudaMemsetAsync(*buf, 0, cb, stream);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+        *region = cb;
+    }
+    *counter_bytes = cb;
+    return B2A_OK;
+}
+
 void inv_freq_table(double theta, int D, double* out) {
     // 1 / theta^(2i/D) in double (INF/decoderonly/DecoderOnlyRotaryEmbedding.java:57-59,
     // INF/gemma/Gemma3ReferenceMath.java:74)
@@ -134,15 +158,9 @@ cudaError_t launch_attention(b2a_context* ctx, const AttnParams& p, cudaStream_t
     size_t part_bytes = 0, counter_ints = 0;
     const int nsplit = attn_simt_split_plan(p, ctx->sm_count, &part_bytes, &counter_ints);
     if (nsplit > 1) {
-        const size_t counter_bytes = (counter_ints * sizeof(int) + 255) / 256 * 256;
-        const bool grow = counter_bytes + part_bytes > ctx->split_ws_bytes;
-        if (ensure_buffer(ctx, &ctx->split_ws, &ctx->split_ws_bytes, counter_bytes + part_bytes, "attention split") ==
-            B2A_OK) {
-            if (grow || counter_ints > ctx->split_counter_ints) {
-                const cudaError_t e = cudaMemsetAsync(ctx->split_ws, 0, counter_bytes, s);
-                if (e != cudaSuccess) return e;
-                ctx->split_counter_ints = counter_bytes / sizeof(int);
-            }
+        size_t counter_bytes = 0;
+        if (ensure_counted_buffer(ctx, &ctx->split_ws, &ctx->split_ws_bytes, &ctx->split_counter_bytes, counter_ints,
+                                  part_bytes, "attention split workspace", s, false, &counter_bytes) == B2A_OK) {
             const SimtSplit sp{reinterpret_cast<float*>(static_cast<char*>(ctx->split_ws) + counter_bytes),
                                static_cast<int*>(ctx->split_ws), nsplit, kSimtSplitKeys};
             return launch_attn_simt(p, s, &sp);
@@ -164,16 +182,10 @@ int run_decode(b2a_context* ctx, DecodeParams& p, cudaStream_t stream, bool allo
         decode_tc_workspace(ctx->device, p.B, p.Hkv, p.n_hg, p.D, p.cache_dtype, &target, &cap, &partial_bytes);
         const int bmax = std::min(p.B, kDecodeMaxBatchPerLaunch);
         const size_t counter_ints = (size_t)bmax * p.Hkv * p.n_hg;
-        const size_t counter_bytes = (counter_ints * sizeof(int) + 255) / 256 * 256;
-        const size_t need = counter_bytes + partial_bytes;
-        const bool grow = need > ctx->dec_ws_bytes;
-        int rc = ensure_buffer(ctx, &ctx->dec_ws, &ctx->dec_ws_bytes, need, "decode");
+        size_t counter_bytes = 0;
+        int rc = ensure_counted_buffer(ctx, &ctx->dec_ws, &ctx->dec_ws_bytes, &ctx->dec_counter_bytes, counter_ints,
+                                       partial_bytes, "decode workspace", stream, false, &counter_bytes);
         if (rc != B2A_OK) return rc;
-        if (grow || counter_ints > ctx->dec_counter_ints) {
-            cudaError_t e = cudaMemsetAsync(ctx->dec_ws, 0, counter_bytes, stream);
-            if (e != cudaSuccess) return cuda_fail(ctx, e, "decode workspace reset");
-            ctx->dec_counter_ints = counter_bytes / sizeof(int);
-        }
         p.counters = static_cast<int*>(ctx->dec_ws);
         p.partials = reinterpret_cast<float*>(static_cast<char*>(ctx->dec_ws) + counter_bytes);
         p.target_items = target;
@@ -314,16 +326,9 @@ B2A_API int b2a_reserve_decode(b2a_context* ctx, int max_batch, int num_q_heads,
     decode_tc_workspace(ctx->device, max_batch, num_kv_heads, n_hg, head_dim, B2A_FLOAT16, &target, &cap,
                         &partial_bytes);
     const size_t counter_ints = (size_t)std::min(max_batch, kDecodeMaxBatchPerLaunch) * num_kv_heads * n_hg;
-    const size_t counter_bytes = (counter_ints * sizeof(int) + 255) / 256 * 256;
-    const bool grow = counter_bytes + partial_bytes > ctx->dec_ws_bytes;
-    rc = ensure_buffer(ctx, &ctx->dec_ws, &ctx->dec_ws_bytes, counter_bytes + partial_bytes, "decode");
-    if (rc) return rc;
-    if (grow || counter_ints > ctx->dec_counter_ints) {
-        cudaError_t e = cudaMemset(ctx->dec_ws, 0, counter_bytes);
-        if (e != cudaSuccess) return cuda_fail(ctx, e, "decode workspace reset");
-        ctx->dec_counter_ints = counter_bytes / sizeof(int);
-    }
-    return B2A_OK;
+    size_t counter_bytes = 0;
+    return ensure_counted_buffer(ctx, &ctx->dec_ws, &ctx->dec_ws_bytes, &ctx->dec_counter_bytes, counter_ints,
+                                 partial_bytes, "decode workspace", nullptr, true, &counter_bytes);
 }
 
 B2A_API int b2a_test_inject_wait_timeout(b2a_context* ctx) {
