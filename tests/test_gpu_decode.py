@@ -79,6 +79,16 @@ def test_decode_gemma_shape_local_and_global(ctx, window, theta):
               rope_mode="gemma", theta=theta, window=window, qk_norm=True, seed=31)
 
 
+def test_decode_equal_units_take_whole_units_per_cta(ctx):
+    """Every unit the same length (contexts past the window) and at least one unit per CTA: CTAs take
+    whole units instead of cutting them (no partial slots, no merges). D = 64 (296 CTAs, 320 units) and a
+    Gemma-local-shaped D = 256 case (148 CTAs, 150 units; QK-norm, Gemma RoPE)."""
+    rng = np.random.default_rng(5)
+    _run_case(ctx, B=160, Hq=4, Hkv=2, D=64, max_seq=320, lens=rng.integers(150, 319, 160), window=100, seed=81)
+    _run_case(ctx, B=150, Hq=4, Hkv=1, D=256, max_seq=200, lens=rng.integers(64, 199, 150), window=64,
+              layout=oracle.KV_POS_MAJOR, rope_mode="gemma", theta=1e4, qk_norm=True, seed=91)
+
+
 def test_decode_batch_sizes_shrinking_and_growing_on_one_context(ctx):
     """The workspace's merge counters must stay zero between calls whatever the batch order: a large batch,
     then a small one whose partial slots must not land where a larger batch keeps counters, then a medium

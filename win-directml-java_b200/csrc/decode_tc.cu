@@ -231,16 +231,30 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
     // that falls on a unit's gap does no work there.
     // prefix[b] = stream length of sequences < b, per unit (int32: the host keeps
     // each launch's total below 2^31).
+    // Unit-aligned ranges instead: when every unit has the same length (a sliding-window
+    // layer whose contexts all exceed the window) and there are at least as many units as
+    // CTAs, CTA c takes whole units [c*U/G, (c+1)*U/G) -- no unit is cut, so no partial
+    // slots and no merges -- unless the uneven unit counts would cost more than the two
+    // pieces' allowance that stream-K charges.
+    int n_min = 0, n_max = 0;
     {
         const int per = (p.B + kThreads - 1) / kThreads;
         const int b0 = min(p.B, tid * per), b1 = min(p.B, b0 + per);
-        int run = 0, bad = 0;
+        int run = 0, bad = 0, lmin = INT32_MAX, lmax = 0;
         for (int b = b0; b < b1; ++b) {
             const int L_in = ctx_len_of(p, b);
             if (Gm::kLensCached) lens_s[b] = L_in;
             int L, first;
             if (!seq_range_of(p, L_in, L, first)) bad = 1;
             run += L - first + 1 + Gm::kGapKeys;
+            lmin = min(lmin, L - first + 1);
+            lmax = max(lmax, L - first + 1);
+        }
+        lmin = __reduce_min_sync(0xffffffffu, lmin);
+        lmax = __reduce_max_sync(0xffffffffu, lmax);
+        if (lane == 0) {
+            misc[4 + warp] = lmin;
+            misc[12 + warp] = lmax;
         }
         if (bad && blockIdx.x == 0) atomicOr(p.status, 1);
         int incl = run;
@@ -262,6 +276,12 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         }
         if (tid == kThreads - 1) prefix[p.B] = warp_off + incl;
         __syncthreads();
+        n_min = misc[4];
+        n_max = misc[12];
+        for (int w = 1; w < kWarps; ++w) {
+            n_min = min(n_min, misc[4 + w]);
+            n_max = max(n_max, misc[12 + w]);
+        }
     }
     const int per_chunk = p.Hkv * p.n_hg;  // units per sequence
     const long long total = (long long)prefix[p.B] * per_chunk;
@@ -273,8 +293,13 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
     const float scale_log2 = p.scale * kLog2e;
     constexpr float kNegInf = -INFINITY;
     const bool small = total <= (long long)INT32_MAX;
-    const long long range_lo = (long long)blockIdx.x * R;
-    const long long range_hi = min(total, range_lo + R);
+    const long long n_units = (long long)p.B * per_chunk, n_cta = gridDim.x;
+    const long long unit_len = (long long)n_max + Gm::kGapKeys;
+    const bool aligned = n_min == n_max && n_units >= n_cta &&
+                         (n_units + n_cta - 1) / n_cta * unit_len <= R + 2 * Gm::kGapKeys;
+    const long long range_lo = aligned ? blockIdx.x * n_units / n_cta * unit_len : (long long)blockIdx.x * R;
+    const long long range_hi =
+        aligned ? (blockIdx.x + 1) * n_units / n_cta * unit_len : min(total, range_lo + R);
 
     for (long long pos = range_lo; pos < range_hi;) {
         // unit containing pos: sequence b (prefix search), then (kv head, head group)
@@ -303,7 +328,7 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         const int k1 = first + (int)(piece_end - u_start);
         const int c0 = small ? (int)u_start / (int)R : (int)(u_start / R);
         const int c1 = small ? (int)(u_end - 1) / (int)R : (int)((u_end - 1) / R);
-        const int n_split = c1 - c0 + 1;                    // pieces of this unit
+        const int n_split = aligned ? 1 : c1 - c0 + 1;      // pieces of this unit
         const int my_slot = 2 * blockIdx.x + (pos == range_lo ? 0 : 1);
         const int unit = b * per_chunk + r;
         pos = piece_end;
