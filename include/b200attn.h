@@ -117,7 +117,9 @@ B2A_API int b2a_abi_version(void);
 B2A_API const char* b2a_build_info(void);
 
 /* Cap on the bytes of device workspace the context may allocate (0 = no
- * cap).  A call whose workspace would exceed it fails with B2A_EOOM. */
+ * cap).  A call whose workspace would exceed it fails with B2A_EOOM, except
+ * for the optional key-split workspace of the generic (fp32 / odd head dim)
+ * attention kernel: without room for it the launch runs unsplit. */
 B2A_API int b2a_set_workspace_limit(b2a_context* ctx, size_t bytes);
 
 /* Bytes of device workspace the context currently holds. */
