@@ -292,3 +292,24 @@ def test_generic_kernel_key_split_back_to_back(ctx):
     for got, want, what in cases:
         err, _ = assert_close(to_np(got), want, what=what)
         assert err < 1e-4, what  # fp32 end to end
+
+
+def test_generic_kernel_runs_unsplit_without_room_for_the_split_workspace():
+    """Under a context workspace limit too small for the key-split workspace, a launch that would split
+    runs unsplit instead of failing, and its results are the same."""
+    import torch
+    import b200attn
+    lens = [200, 60]
+    shape = (2, 2, 200, 64)  # head-major fp32 encoder: needs no staging, would split (few query blocks)
+    q, k, v = (normal(760 + j, shape, oracle.F32) for j in range(3))
+    want = oracle.encoder_minilm(q, k, v, lens, B=2, H=2, S=200, D=64, layout=0)
+    with b200attn.Context(0) as small:
+        small.set_workspace_limit(4096)
+        y = torch.full(shape, float("nan"), dtype=torch.float32, device="cuda")
+        b200attn.mha(small, to_dev(q, oracle.F32), to_dev(k, oracle.F32), to_dev(v, oracle.F32), y, 1.0 / 8.0,
+                     key_lengths=torch.from_numpy(np.asarray(lens, np.int32)).cuda(), layout=b200attn.HEAD_MAJOR)
+        torch.cuda.synchronize()
+        small.check_device_status()
+        assert small.workspace_bytes() <= 4096
+        err, _ = assert_close(to_np(y), want, what="unsplit fp32 encoder under a workspace limit")
+        assert err < 1e-4
