@@ -168,13 +168,29 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ workloads
+DECODE_SHAPES = {  # B per GPU, Hq, Hkv, D, context range, layers (window, RoPE theta)
+    "c5": dict(B=256, Hq=4, Hkv=1, D=256, lo=1024, hi=32768, layers=[(512, 1e4), (0, 1e6)]),
+    "c3": dict(B=64, Hq=14, Hkv=2, D=64, lo=512, hi=8192, layers=[(0, 1e6)]),
+}
+
+
+def decode_config(name: str, B: int, lens, max_seq: int) -> dict:
+    """The `config` object of a decode workload's JSON line (both arms print the same one)."""
+    sh = DECODE_SHAPES[name]
+    cache_gb = len(sh["layers"]) * 2 * B * max_seq * sh["Hkv"] * sh["D"] * 2 / 1e9
+    return {"workload": WORKLOADS[name], "batch_per_gpu": B, "q_heads": sh["Hq"], "kv_heads": sh["Hkv"],
+            "head_dim": sh["D"], "ctx_len": f"U[{sh['lo']},{sh['hi']}]", "mean_ctx": float(np.mean(lens)),
+            "layers_per_step": [("local W%d" % w) if w else "global" for w, _ in sh["layers"]],
+            "kv_dtype": "f16", "l2": "inputs larger than L2 (KV caches %.1f GB)" % cache_gb}
+
+
 class DecodeWorkload:
     """configs[4] (c5) or configs[2] (c3): one decode token for every sequence."""
 
     def __init__(self, name: str, seed: int, batch: int = 0, world: int = 1, rank: int = 0):
         import torch
         import b200attn
-        self.torch, self.b2a = torch, b200attn
+        self.torch, self.b2a, self.name = torch, b200attn, name
         if name == "c5":
             self.B, self.Hq, self.Hkv, self.D, self.lo, self.hi = 256, 4, 1, 256, 1024, 32768
             self.layers = [dict(window=512, theta=1e4), dict(window=0, theta=1e6)]
@@ -185,10 +201,10 @@ class DecodeWorkload:
             self.layout, self.rope, self.norm = b200attn.KV_HEAD_MAJOR, b200attn.ROPE_NEOX, False
         if batch > 0:  # smaller batch for profiler captures only
             self.B = batch
-        import oracle
+        from b200attn import synthetic
         # one global batch of world * B sequences; each rank takes its cost-balanced,
         # equal-count shard (b200attn.sharding.plan_shards; cost = keys attended)
-        lens_all = oracle.splitmix_uniform_int(seed, self.B * world, self.lo, self.hi)
+        lens_all = synthetic.uniform_int(seed, self.B * world, self.lo, self.hi)
         if world > 1:
             from b200attn import sharding
             self.lens = np.ascontiguousarray(lens_all[sharding.plan_shards(lens_all.astype(np.int64) + 1, world)[rank]])
@@ -274,11 +290,7 @@ class DecodeWorkload:
         return h2d, d2h
 
     def config(self):
-        return {"batch_per_gpu": self.B, "q_heads": self.Hq, "kv_heads": self.Hkv, "head_dim": self.D,
-                "ctx_len": f"U[{self.lo},{self.hi}]", "mean_ctx": float(self.lens.mean()),
-                "layers_per_step": [("local W%d" % l["window"]) if l["window"] else "global" for l in self.layers],
-                "kv_dtype": "f16", "l2": "inputs larger than L2 (KV caches %.1f GB)" % (
-                    sum(t.numel() * 2 for c in self.caches for t in c) / 1e9)}
+        return decode_config(self.name, self.B, self.lens, self.max_seq)
 
 
 class PrefillWorkload:
@@ -287,7 +299,7 @@ class PrefillWorkload:
     def __init__(self, name: str, seed: int, batch: int = 0):
         import torch
         import b200attn
-        import oracle
+        from b200attn import synthetic
         self.torch, self.b2a, self.name = torch, b200attn, name
         g = torch.Generator(device="cuda").manual_seed(seed)
         if name == "c1":
@@ -296,7 +308,7 @@ class PrefillWorkload:
             self.B, self.S, self.Hq, self.Hkv, self.D, self.dt, self.theta = 8, 4096, 32, 32, 96, torch.bfloat16, 1e4
         else:
             self.B, self.S, self.Hq, self.Hkv, self.D, self.dt, self.theta = 64, 128, 12, 12, 32, torch.float16, 0
-            self.lens = oracle.splitmix_uniform_int(seed, self.B if batch <= 0 else batch, 16, 128)
+            self.lens = synthetic.uniform_int(seed, self.B if batch <= 0 else batch, 16, 128)
             self.lens_d = torch.from_numpy(self.lens).cuda()
         if batch > 0:  # smaller batch for profiler captures only
             self.B = batch
@@ -409,20 +421,26 @@ def run_suite(ctx, hbm, tflops, src):
 
 # ------------------------------------------------------------------ CPU reference arm
 class CpuDecodeSample:
-    """n_seq sequences of the c5 workload held as float32 arrays for the CPU
-    restatement (OpenMP over all host threads); one step = local + global layer."""
+    """A bounded sample of the c5 workload for the CPU restatement (OpenMP over all host
+    threads): n_seq of the benchmark's 256 sequences, taken at the midpoints of n_seq equal
+    quantile bins of their context lengths so that the sample's length mix (and mean) is the
+    whole batch's, in the GPU arm's position-major cache layout; one step = one decode token
+    per sampled sequence through the local W512 and the global layer."""
 
     def __init__(self, n_seq: int, seed: int = 5):
         import oracle
+        from b200attn import synthetic
         self.oracle = oracle
+        sh = DECODE_SHAPES["c5"]
+        self.all_lens = synthetic.uniform_int(seed, sh["B"], sh["lo"], sh["hi"])
+        self.lens = np.ascontiguousarray(self.all_lens[synthetic.stratified_sample(self.all_lens, n_seq)])
         self.n = n_seq
-        self.lens = oracle.splitmix_uniform_int(seed, 256, 1024, 32768)[:n_seq].astype(np.int32)
-        self.D, self.Hq, self.Hkv = 256, 4, 1
+        self.D, self.Hq, self.Hkv = sh["D"], sh["Hq"], sh["Hkv"]
         self.max_seq = int(self.lens.max()) + 1
         rng = np.random.default_rng(seed)
-        shape = (n_seq, self.Hkv, self.max_seq, self.D)
+        shape = (n_seq, self.max_seq, self.Hkv, self.D)  # position-major, as the GPU arm's caches
         self.caches = []
-        for _ in range(2):  # one cache per layer, as on the GPU
+        for _ in sh["layers"]:  # one cache per layer, as on the GPU
             kc = oracle.round_to(rng.standard_normal(shape, dtype=np.float32), oracle.F16).reshape(shape)
             vc = oracle.round_to(rng.standard_normal(shape, dtype=np.float32), oracle.F16).reshape(shape)
             self.caches.append((kc, vc))
@@ -431,17 +449,25 @@ class CpuDecodeSample:
         self.w = (0.5 * rng.standard_normal(self.D)).astype(np.float32)
         self.threads = oracle.max_threads()
 
+    def describe(self) -> str:
+        return (f"{self.n} of the 256 sequences (stratified by context length: sample mean "
+                f"{self.lens.mean():.0f} vs batch mean {self.all_lens.mean():.0f}), position-major fp16-valued "
+                f"caches, one local W512 + one global layer per step")
+
     def step(self):
         o = self.oracle
-        for (kc, vc), (window, theta) in zip(self.caches, ((512, 1e4), (0, 1e6))):
+        for (kc, vc), (window, theta) in zip(self.caches, DECODE_SHAPES["c5"]["layers"]):
             o.decode(self.q, self.kn, self.vn, kc, vc, self.lens, B=self.n, Hq=self.Hq, Hkv=self.Hkv, D=self.D,
                      max_seq=self.max_seq, scale=1 / 16, rope_theta=theta, rope_mode=o.ROPE_GEMMA, window=window,
-                     cache_layout=o.KV_HEAD_MAJOR, q_norm_w=self.w, k_norm_w=self.w,
+                     cache_layout=o.KV_POS_MAJOR, q_norm_w=self.w, k_norm_w=self.w,
                      softmax_mode=o.SOFTMAX_GEMMA, n_threads=self.threads, inplace=True)
 
 
+CPU_SAMPLE_SEQS = 16
+
+
 def cpu_decode_sample(n_seq: int, max_seconds: float = 12.0):
-    """Times the CPU restatement on a bounded sample; returns (tokens/s, threads, seconds, steps)."""
+    """Times the CPU restatement on a bounded sample; returns (tokens/s, threads, seconds, steps, sample)."""
     smp = CpuDecodeSample(n_seq)
     smp.step()  # warm caches / thread pool
     steps, t0 = 0, time.perf_counter()
@@ -451,33 +477,40 @@ def cpu_decode_sample(n_seq: int, max_seconds: float = 12.0):
         el = time.perf_counter() - t0
         if el >= max_seconds or steps >= 200:
             break
-    return n_seq * steps / el, smp.threads, el, steps
+    return n_seq * steps / el, smp.threads, el, steps, smp.describe()
 
 
 def reference_arm(args):
+    """The reference arm: the reference's CPU attention restated in C (no JDK exists here), timed on
+    the host's cores on a bounded sample of the c5 workload; the same metric, unit and config as the
+    GPU arm.  Under torchrun only rank 0 runs it."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     import oracle
+    from b200attn import synthetic
     oracle.build()
-    n_seq = 8
-    smp = CpuDecodeSample(n_seq)
+    smp = CpuDecodeSample(CPU_SAMPLE_SEQS)
+    # each step is the bounded sample; keep the whole run within a few minutes
+    steps = max(1, min(args.steps, 200))
     for _ in range(args.warmup):
         smp.step()
     times = []
-    for _ in range(args.steps):
+    for _ in range(steps):
         t0 = time.perf_counter()
         smp.step()
         times.append(time.perf_counter() - t0)
     ms = 1e3 * statistics.mean(times)
-    value = n_seq / (ms / 1e3)
+    value = smp.n / (ms / 1e3)
     threads = oracle.max_threads()
-    sample = f"{n_seq} of 256 sequences of {WORKLOADS['c5']}, one local + one global layer per step"
+    sh = DECODE_SHAPES["c5"]
+    config = dict(decode_config("c5", sh["B"], synthetic.uniform_int(5, sh["B"] * args.gpus, sh["lo"], sh["hi"]),
+                                sh["hi"] + 1), parallelism=f"shard{args.gpus} (sequences per rank)")
+    sample = smp.describe()
     line = {"metric": "decode tokens/s", "value": round(value, 3), "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "impl": "reference",
-            "config": {"workload": WORKLOADS["c5"], "sample": sample},
+            "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1))",
+            "impl": "reference", "config": config,
             "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
                              "sample": sample + "; C restatement of the reference's Java CPU attention "
                                                 "(no JDK on this machine)"},
@@ -490,7 +523,7 @@ def reference_arm(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="c5", choices=sorted(WORKLOADS))
@@ -612,10 +645,16 @@ def main():
         roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tflops, "unit": "TFLOP/s",
                 "frac": round(achieved / tflops, 4), "peak_source": src + " (bf16_tflops, burst)",
                 "flops_per_step": w.flops(), "traffic": None}
+    # DRAM traffic: ncu's dram__bytes_read + write cannot be read inside a timed run, so the committed
+    # capture's ratio of traffic to algorithmic bytes is applied to this run's algorithmic bytes
     traffic_file = os.path.join(REPO, "profiles", f"decode_tc_kernel_{args.workload}_traffic.txt")
-    if os.path.exists(traffic_file):
+    if isinstance(w, DecodeWorkload) and os.path.exists(traffic_file):
         try:
-            roof["traffic"] = json.load(open(traffic_file)).get("dram_bytes_per_step")
+            ratio = float(json.load(open(traffic_file))["traffic_over_algorithmic"])
+            roof["traffic"] = int(round(ratio * w.algorithmic_bytes()))
+            roof["traffic_source"] = (f"scaled: {ratio} x this step's algorithmic bytes, the ratio of "
+                                      f"profiles/{os.path.basename(traffic_file)} (ncu dram__bytes_read.sum + "
+                                      "dram__bytes_write.sum)")
         except Exception:
             pass
 
@@ -624,9 +663,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16" if isinstance(w, DecodeWorkload) else str(w.dt).split(".")[-1],
             "data": "synthetic (seeded N(0,1); no dataset or checkpoint)",
-            "config": dict({"workload": WORKLOADS[args.workload], "parallelism": f"shard{world} (sequences per rank)",
-                            "launch": launch_mode},
-                           **(w.config() if isinstance(w, DecodeWorkload) else {})),
+            "config": dict(w.config() if isinstance(w, DecodeWorkload) else {"workload": WORKLOADS[args.workload]},
+                           parallelism=f"shard{world} (sequences per rank)", launch=launch_mode),
             "roofline": roof,
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
@@ -634,10 +672,10 @@ def main():
             "clocks": clocks}
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tps, threads, secs, steps = cpu_decode_sample(16, max_seconds=12.0)
+        tps, threads, secs, steps, sample = cpu_decode_sample(CPU_SAMPLE_SEQS, max_seconds=12.0)
         line["cpu_baseline"] = {"value": round(tps, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
-                                "sample": f"16 of 256 sequences of the c5 workload, {steps} step(s) in {secs:.1f} s; "
-                                          "C restatement of the reference's Java CPU attention (no JDK here)"}
+                                "sample": f"{sample}, {steps} step(s) in {secs:.1f} s; C restatement of the "
+                                          "reference's Java CPU attention (no JDK here)"}
     if rank == 0 and world == 1 and not args.no_suite:
         line["suite"] = run_suite(ctx, hbm, tflops, src)
     if rank == 0:

@@ -50,7 +50,7 @@ typedef enum b2a_status {
     B2A_EINVAL = 1,   /* bad shape, dtype, head divisibility, null or misaligned pointer */
     B2A_ECUDA = 2,    /* a CUDA runtime call failed */
     B2A_ENCCL = 3,    /* reserved for collective failures */
-    B2A_ETIMEOUT = 4, /* a bounded device-side wait ran out */
+    B2A_ETIMEOUT = 4, /* a bounded device-side wait ran out (b2a_check_device_status) */
     B2A_EOOM = 5,     /* device allocation failed or exceeded the context's cap */
     B2A_ENOTSUP = 6,  /* valid arguments, but no kernel for this combination */
     B2A_EDEVICE = 7   /* a device-side argument check failed (see b2a_check_device_status) */
@@ -130,9 +130,18 @@ B2A_API int b2a_workspace_bytes(const b2a_context* ctx, size_t* bytes);
 B2A_API int b2a_reserve_decode(b2a_context* ctx, int max_batch, int num_q_heads, int num_kv_heads,
                                int head_dim);
 
-/* Synchronise `stream` and report device-side argument checks raised since
- * the last call (for example a ctx_lens entry outside [0, max_seq)).
- * Returns B2A_OK or B2A_EDEVICE and clears the flag. */
+/* Synchronise `stream` and report what the context's kernels flagged on the
+ * device since the last call, then clear it:
+ *   B2A_ETIMEOUT  a bounded device-side wait ran out and the launch aborted
+ *                 (its outputs are undefined); takes precedence over the others;
+ *   B2A_EDEVICE   a device-side argument check failed (a ctx_lens entry outside
+ *                 [0, max_seq), a bf16 input beyond the fp16 operand range);
+ *   B2A_OK        nothing was flagged.
+ * The compute calls are asynchronous, as CUDA launches are; a binding that
+ * mirrors the reference's synchronous dispatch (DirectMlAttentionKernel.dispatch
+ * waits on a fence unless a DirectMlGpuBatch is open, WB/windows/D3D12Bindings.java:921-937)
+ * calls this after each dispatch, or once when its batch closes, and throws on
+ * a non-zero status. */
 B2A_API int b2a_check_device_status(b2a_context* ctx, void* stream);
 
 /* ------------------------------------------------------------ encoder MHA */
@@ -218,6 +227,11 @@ B2A_API int b2a_decode(b2a_context* ctx, int q_dtype, int cache_dtype, int out_d
  * caches, head_dim 64/96/128/256, batch <= 2048 and
  * batch * Hkv * ceil((Hq/Hkv)/8) <= 16384; larger requests fail with
  * B2A_EINVAL / B2A_ENOTSUP and a message in b2a_last_error(NULL, ...).
+ * The split-KV partial slots take 2 * grid * 8 * (head_dim + 2) * 4 bytes of
+ * the array, grid being the decode kernel's resident CTAs (SMs x CTAs per SM
+ * for that head dim): on a B200 (148 SMs) every supported head dim fits (at
+ * most about 2.5 MB); a GPU with more resident CTAs can exceed it, and then
+ * every call at that head dim returns B2A_ENOTSUP.
  * All calls share the scratch: calls whose kernels overlap on the GPU race,
  * so serialise them (one stream).  An out-of-range ctx_lens entry gives NaN
  * outputs for that sequence; there is no device-status query. */

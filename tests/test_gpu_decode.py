@@ -165,3 +165,84 @@ def test_decode_full_size_qwen_config(ctx):
     """configs[2] at full size: B=64, 14/2, D=64, fp16 cache, ctx ~ U[512, 8192]."""
     lens = oracle.splitmix_uniform_int(3, 64, 512, 8192)
     _run_case(ctx, B=64, Hq=14, Hkv=2, D=64, max_seq=8193, lens=lens, theta=1e6, seed=3000)
+
+
+def _long_context_case(ctx, *, lens, Hq, Hkv, D, max_seq, layout, rope_mode, theta, window, qk_norm, seed,
+                       q_dtype=oracle.F16, cache_dtype=oracle.F16):
+    """Parity at the benchmarked context lengths.  The caches are too large for the splitmix generator
+    and for whole-cache comparisons, so they are drawn with numpy's seeded normal generator (rounded to
+    the cache type), the output is compared with the oracle, the appended rows are compared within one
+    ulp, and every other row is checked unchanged through a per-sequence checksum."""
+    import torch
+    import b200attn
+    B = len(lens)
+    lens = np.asarray(lens, np.int32)
+    rng = np.random.default_rng(seed)
+    q = normal(seed, (B, Hq, D), q_dtype)
+    kn = normal(seed + 1, (B, Hkv, D), q_dtype)
+    vn = normal(seed + 2, (B, Hkv, D), q_dtype)
+    shape = (B, Hkv, max_seq, D) if layout == oracle.KV_HEAD_MAJOR else (B, max_seq, Hkv, D)
+    assert cache_dtype == oracle.F16  # numpy's float16 cast rounds to nearest even, as the cache type does
+    kc = rng.standard_normal(shape, dtype=np.float32).astype(np.float16).astype(np.float32)
+    vc = rng.standard_normal(shape, dtype=np.float32).astype(np.float16).astype(np.float32)
+    qw = kw = None
+    if qk_norm:
+        qw = (0.5 * normal(seed + 5, (D,), oracle.F32)).astype(np.float32)
+        kw = (0.5 * normal(seed + 6, (D,), oracle.F32)).astype(np.float32)
+    kc_d, vc_d = to_dev(kc, cache_dtype), to_dev(vc, cache_dtype)
+    sums_before = [(kc_d[b].double().sum().item(), vc_d[b].double().sum().item()) for b in range(B)]
+    scale = float(np.float32(1.0 / np.sqrt(D)))
+    out = torch.empty((B, Hq, D), dtype=torch.float32, device="cuda")
+    b200attn.decode(ctx, to_dev(q, q_dtype), to_dev(kn, q_dtype), to_dev(vn, q_dtype), kc_d, vc_d,
+                    torch.from_numpy(lens).cuda(), out, scale,
+                    kv_layout=b200attn.KV_HEAD_MAJOR if layout == oracle.KV_HEAD_MAJOR else b200attn.KV_POS_MAJOR,
+                    rope_mode=b200attn.ROPE_GEMMA if rope_mode == "gemma" else b200attn.ROPE_NEOX,
+                    rope_theta=theta, window=window,
+                    q_norm_w=None if qw is None else torch.from_numpy(qw).cuda(),
+                    k_norm_w=None if kw is None else torch.from_numpy(kw).cuda(), norm_eps=1e-6)
+    ctx.check_device_status()
+    # the oracle appends in place into the host caches (the device copies were taken above)
+    old_rows = [(kc[b, :, L].copy(), vc[b, :, L].copy()) if layout == oracle.KV_HEAD_MAJOR else
+                (kc[b, L].copy(), vc[b, L].copy()) for b, L in enumerate(lens)]
+    want, _, _ = oracle.decode(
+        q, kn, vn, kc, vc, lens, B=B, Hq=Hq, Hkv=Hkv, D=D, max_seq=max_seq, scale=scale, rope_theta=theta,
+        rope_mode=oracle.ROPE_GEMMA if rope_mode == "gemma" else oracle.ROPE_DECODERONLY, window=window,
+        cache_layout=layout, cache_dtype=cache_dtype, q_norm_w=qw, k_norm_w=kw, norm_eps=1e-6,
+        softmax_mode=oracle.SOFTMAX_GEMMA if rope_mode == "gemma" else oracle.SOFTMAX_DECODERONLY, inplace=True)
+    err, cos = assert_close(to_np(out), want, what="long-context decode output")
+    ulp = {oracle.F16: 2 ** -10, oracle.BF16: 2 ** -7}[cache_dtype]
+    for b, L in enumerate(lens):
+        if layout == oracle.KV_HEAD_MAJOR:
+            got_k, got_v, want_k, want_v = to_np(kc_d[b, :, L]), to_np(vc_d[b, :, L]), kc[b, :, L], vc[b, :, L]
+        else:
+            got_k, got_v, want_k, want_v = to_np(kc_d[b, L]), to_np(vc_d[b, L]), kc[b, L], vc[b, L]
+        np.testing.assert_allclose(got_k, want_k, rtol=ulp, atol=1e-6)
+        np.testing.assert_array_equal(got_v, want_v)
+        # rows other than L unchanged: the sequence's sum moved by exactly (new row - old row)
+        dk = float(got_k.astype(np.float64).sum() - old_rows[b][0].astype(np.float64).sum())
+        dv = float(got_v.astype(np.float64).sum() - old_rows[b][1].astype(np.float64).sum())
+        assert abs(kc_d[b].double().sum().item() - (sums_before[b][0] + dk)) < 1e-6
+        assert abs(vc_d[b].double().sum().item() - (sums_before[b][1] + dv)) < 1e-6
+    return err, cos
+
+
+@pytest.mark.parametrize("window,theta", [(512, 1e4), (0, 1e6)])
+def test_decode_gemma_config_full_context_range(ctx, window, theta):
+    """configs[4] at its real context lengths: 12 of the benchmark's sequences (contexts drawn from
+    U[1024, 32768] with the bench seed, the shortest and longest among them) plus one at the maximum
+    32768, 4/1 heads, D = 256, QK-norm, Gemma RoPE, fp16 position-major cache; the local W512 / theta 1e4
+    layer and the global theta 1e6 layer."""
+    all_lens = oracle.splitmix_uniform_int(5, 256, 1024, 32768)
+    order = np.argsort(all_lens)
+    pick = order[np.linspace(0, 255, 12).astype(int)]
+    lens = np.concatenate([all_lens[pick], [32768]]).astype(np.int32)
+    _long_context_case(ctx, lens=lens, Hq=4, Hkv=1, D=256, max_seq=32769, layout=oracle.KV_POS_MAJOR,
+                       rope_mode="gemma", theta=theta, window=window, qk_norm=True, seed=5000 + window)
+
+
+def test_decode_qwen_config_longest_contexts(ctx):
+    """configs[2] geometry at the top of its context range, 8192 included (14/2 heads, D = 64,
+    head-major fp16 cache, NeoX RoPE theta 1e6)."""
+    lens = np.array([8192, 8191, 7000, 512, 4096, 8000], np.int32)
+    _long_context_case(ctx, lens=lens, Hq=14, Hkv=2, D=64, max_seq=8193, layout=oracle.KV_HEAD_MAJOR,
+                       rope_mode="neox", theta=1e6, window=0, qk_norm=False, seed=5100)

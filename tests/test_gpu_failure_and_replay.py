@@ -2,8 +2,11 @@
 
 * A bounded wait inside the tensor-core prefill kernel is made to run out (the test
   hook of include/b200attn_testing.h leaves one K/V copy unissued): the launch
-  returns, the device status reports it (B2A_EDEVICE), and the same context then
-  computes correct results.
+  returns, the device status reports it (B2A_ETIMEOUT), and the same context then
+  computes correct results -- also when the next launch comes before anyone read
+  the status.  The AttentionKernel mirror raises at the dispatch (or when its
+  GpuBatch closes) instead of returning undefined output.
+* A decode whose workspace would exceed the context's limit fails with B2A_EOOM.
 * The persistent prefill takes work items from a counter that its last CTA resets:
   back-to-back launches with different item counts, and CUDA-graph replays of one
   launch, must each compute every item.
@@ -43,7 +46,7 @@ def test_bounded_wait_timeout_is_reported_and_the_context_stays_usable(ctx):
     torch.cuda.synchronize()  # the launch ends: its roles gave up after the bounded wait
     with pytest.raises(b200attn.B200RuntimeException) as ei:
         ctx.check_device_status()
-    assert ei.value.status == b200attn.B2A_EDEVICE
+    assert ei.value.status == b200attn.B2A_ETIMEOUT
     assert "bounded device wait ran out" in str(ei.value)
     ctx.check_device_status()  # reading the status cleared it
     # the context, its workspaces and the work-item counter are intact
@@ -52,6 +55,77 @@ def test_bounded_wait_timeout_is_reported_and_the_context_stays_usable(ctx):
     torch.cuda.synchronize()
     ctx.check_device_status()
     assert_close(to_np(o), want, what="prefill after a timed-out launch")
+
+
+def test_launch_after_a_timed_out_one_runs_normally_before_the_status_is_read(ctx):
+    """The abort of a timed-out launch is per launch: the next launch, queued before anyone read the
+    status, computes every item; the timeout is still reported afterwards."""
+    import torch
+    import b200attn
+    B, S, Hq, Hkv, D = 2, 640, 4, 2, 96
+    q, k, v, scale, want = _prefill_inputs(B, S, Hq, Hkv, D, seed=37)
+    qd, kd, vd = to_dev(q, oracle.F16), to_dev(k, oracle.F16), to_dev(v, oracle.F16)
+    o1 = torch.empty((B, S, Hq, D), dtype=torch.float32, device="cuda")
+    o2 = torch.full((B, S, Hq, D), float("nan"), dtype=torch.float32, device="cuda")
+    ctx.check_device_status()
+    ctx.inject_wait_timeout()
+    b200attn.prefill_causal(ctx, qd, kd, vd, o1, scale, rope_mode=b200attn.ROPE_NEOX, rope_theta=1e4)
+    b200attn.prefill_causal(ctx, qd, kd, vd, o2, scale, rope_mode=b200attn.ROPE_NEOX, rope_theta=1e4)
+    torch.cuda.synchronize()
+    assert_close(to_np(o2), want, what="launch queued behind a timed-out one")
+    with pytest.raises(b200attn.B200RuntimeException) as ei:
+        ctx.check_device_status()
+    assert ei.value.status == b200attn.B2A_ETIMEOUT
+
+
+def test_attention_kernel_dispatch_raises_on_a_device_timeout(ctx):
+    """CudaAttentionKernel.dispatch outside a batch waits and raises (the reference's dispatch waits on
+    its fence); inside a GpuBatch the dispatch returns and the batch's close raises."""
+    import torch
+    import b200attn
+    B, H, S, D = 1, 2, 256, 64  # fp16 head-major, head dim 64: the tcgen05 kernel
+    shape = (B, H, S, D)
+    q, k, v = (to_dev(normal(80 + i, shape, oracle.F16), oracle.F16) for i in range(3))
+    y = torch.empty(shape, dtype=torch.float32, device="cuda")
+    kern = b200attn.CudaAttentionKernel(ctx, B, H, S, D, 0.125, False)
+    ctx.check_device_status()
+    ctx.inject_wait_timeout()
+    with pytest.raises(b200attn.B200RuntimeException) as ei:
+        kern.dispatch(q, k, v, None, y, 0.125)
+    assert ei.value.status == b200attn.B2A_ETIMEOUT
+    kern.dispatch(q, k, v, None, y, 0.125)  # the context recovered
+    ctx.inject_wait_timeout()
+    with pytest.raises(b200attn.B200RuntimeException) as ei:
+        with b200attn.GpuBatch.begin(ctx):
+            kern.dispatch(q, k, v, None, y, 0.125)  # returns at once
+            with b200attn.GpuBatch.begin(ctx):  # nested: shares the outer batch
+                kern.dispatch(q, k, v, None, y, 0.125)
+    assert ei.value.status == b200attn.B2A_ETIMEOUT
+    assert b200attn.GpuBatch.current() is None
+    ctx.check_device_status()
+
+
+def test_decode_workspace_beyond_the_context_limit_is_b2a_eoom():
+    """The decode's split workspace counts against the context's cap: a cap below it fails the call with
+    B2A_EOOM (the reference has no cap; its allocation failures surface as DirectMlRuntimeException)."""
+    import torch
+    import b200attn
+    B, Hq, Hkv, D, S = 4, 8, 2, 64, 256
+    z = lambda *s: torch.zeros(*s, dtype=torch.float16, device="cuda")
+    lens = torch.full((B,), 100, dtype=torch.int32, device="cuda")
+    out = torch.empty(B, Hq, D, device="cuda")
+    with b200attn.Context(0) as small:
+        small.set_workspace_limit(1024)
+        with pytest.raises(b200attn.B200RuntimeException) as ei:
+            b200attn.decode(small, z(B, Hq, D), z(B, Hkv, D), z(B, Hkv, D), z(B, Hkv, S, D), z(B, Hkv, S, D), lens,
+                            out, 0.125)
+        assert ei.value.status == b200attn.B2A_EOOM
+        assert "exceeds the context limit" in str(ei.value)
+        assert small.workspace_bytes() <= 1024
+        small.set_workspace_limit(0)  # no cap: the same call runs
+        b200attn.decode(small, z(B, Hq, D), z(B, Hkv, D), z(B, Hkv, D), z(B, Hkv, S, D), z(B, Hkv, S, D), lens,
+                        out, 0.125)
+        small.check_device_status()
 
 
 def test_persistent_prefill_back_to_back_launches_with_different_item_counts(ctx):

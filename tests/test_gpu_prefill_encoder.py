@@ -53,6 +53,20 @@ def test_prefill_bf16_output_within_tolerance_plus_rounding(ctx):
     assert np.all(np.abs(got - want) <= 2e-3 + half_ulp)
 
 
+@pytest.mark.parametrize("out_dtype", [oracle.F32, oracle.BF16])
+def test_prefill_phi3_config_full_sequence(ctx, out_dtype):
+    """configs[3] at its full sequence length: S = 4096, D = 96, MHA, NeoX RoPE theta 1e4, bf16 inputs, on
+    a 2-head slice of one sequence (every query tile, the whole causal triangle, positions up to 4095).
+    fp32 output: the 2e-3 / 0.9999 bar; bf16 output: 2e-3 plus half a bf16 ulp of the oracle value."""
+    got, want = _prefill_case(ctx, B=1, S=4096, Hq=2, Hkv=2, D=96, dtype=oracle.BF16, out_dtype=out_dtype,
+                              theta=1e4, seed=4096)
+    if out_dtype == oracle.F32:
+        assert_close(got, want, what="phi3 S=4096 prefill (fp32 out)")
+    else:
+        half_ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(want), 2.0 ** -126))) - 8)
+        assert np.all(np.abs(got - want) <= 2e-3 + half_ulp), float(np.max(np.abs(got - want) - half_ulp))
+
+
 def test_prefill_head_dim_256_tensor_cores(ctx):
     """head_dim 256 (Gemma-3): one 128-row query tile per work item on the tcgen05 kernel, causal GQA over
     several key tiles with a ragged last one."""

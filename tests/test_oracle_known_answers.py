@@ -155,3 +155,18 @@ def test_dtype_rounding_matches_numpy_fp16():
 def test_bf16_rounding_is_nearest_even():
     x = np.array([1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -3.14159], np.float32)
     np.testing.assert_array_equal(oracle.round_to(x, oracle.BF16), np.array([1.0, 1.015625, -3.140625], np.float32))
+
+
+def test_benchmark_generators_match_the_oracles():
+    """The benchmark draws its inputs with b200attn.synthetic (so its GPU arm never loads the oracle); the
+    values must be the ones the oracle's generators give the parity tests."""
+    from b200attn import synthetic
+    np.testing.assert_array_equal(synthetic.uniform_int(5, 256, 1024, 32768),
+                                  oracle.splitmix_uniform_int(5, 256, 1024, 32768))
+    np.testing.assert_array_equal(synthetic.uniform_int(2, 64, 16, 128, offset=3),
+                                  oracle.splitmix_uniform_int(2, 64, 16, 128, offset=3))
+    np.testing.assert_array_equal(synthetic.normal(7, 1000, offset=11), oracle.splitmix_normal(7, 1000, offset=11))
+    lens = synthetic.uniform_int(5, 256, 1024, 32768)
+    pick = synthetic.stratified_sample(lens, 16)
+    assert len(set(pick.tolist())) == 16
+    assert abs(lens[pick].mean() / lens.mean() - 1) < 0.03

@@ -86,3 +86,38 @@ def test_two_gloo_ranks_reassemble_the_single_process_result():
     for rank, _, full, slowest in results:
         np.testing.assert_array_equal(full, want)  # per-sequence work is independent: bit-exact
         assert slowest == [2.0, 10.0]
+
+
+def _bad_count_rank(rank, claimed_world, port, result_q):
+    """A rank that joins a group whose declared size is larger than the ranks that exist."""
+    from datetime import timedelta
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=claimed_world, timeout=timedelta(seconds=4))
+        result_q.put((rank, "joined"))
+        dist.destroy_process_group()
+    except Exception as e:  # the rendezvous gives up: the failure surfaces on the host as an exception
+        result_q.put((rank, type(e).__name__))
+
+
+def test_group_init_with_a_bad_rank_count_fails_on_the_host_within_its_timeout():
+    """Failure detection on the host: two processes start a group that declares three ranks.  The
+    rendezvous never completes, and each rank gets an exception within the group's timeout instead of
+    hanging (the same holds for NCCL, whose init goes through the same rendezvous)."""
+    import time
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_bad_count_rank, args=(r, 3, port, q)) for r in range(2)]
+    t0 = time.time()
+    for pr in procs:
+        pr.start()
+    results = dict(q.get(timeout=120) for _ in range(2))
+    for pr in procs:
+        pr.join(timeout=60)
+        assert pr.exitcode == 0
+    assert set(results) == {0, 1}
+    assert all(v != "joined" for v in results.values()), results
+    assert time.time() - t0 < 110

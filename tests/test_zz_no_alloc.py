@@ -3,10 +3,11 @@
 Some hosts own all device memory through their own arena or caching pool (a
 JVM or serving runtime); for them a cudaMalloc inside the library can fail or
 stall the device.  This entry point takes no context and uses a static device
-scratch instead.  The test calls it through the C ABI twice in a row and
-checks both results against the regular b2a_decode on identical inputs, with
-the parity tolerance used everywhere else (max abs 2e-3, cosine 0.9999).
-It lives in its own file so that pytest collects it last.
+scratch instead.  The tests call it through the C ABI twice in a row and check
+both results against the regular b2a_decode on identical inputs and against
+the CPU oracle, with the parity tolerance used everywhere else (max abs 2e-3,
+cosine 0.9999); they also check that the calls leave the device's free memory
+unchanged.  The file is named so that pytest collects it last.
 """
 import ctypes
 
@@ -28,45 +29,76 @@ def _noalloc_fn():
     return f
 
 
-def _case(ctx, *, B, Hq, Hkv, D, max_seq, lens, layout, rope, theta, window, norm, seed):
+def _case(ctx, *, B, Hq, Hkv, D, max_seq, lens, layout, rope, theta, window, norm, seed, dtype=oracle.F16):
     import torch
     import b200attn
     ptr = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
-    q = to_dev(normal(seed, (B, Hq, D), oracle.F16), oracle.F16)
-    kn = to_dev(normal(seed + 1, (B, Hkv, D), oracle.F16), oracle.F16)
-    vn = to_dev(normal(seed + 2, (B, Hkv, D), oracle.F16), oracle.F16)
+    qh, knh, vnh = normal(seed, (B, Hq, D), dtype), normal(seed + 1, (B, Hkv, D), dtype), \
+        normal(seed + 2, (B, Hkv, D), dtype)
+    q, kn, vn = to_dev(qh, dtype), to_dev(knh, dtype), to_dev(vnh, dtype)
     shape = (B, Hkv, max_seq, D) if layout == b200attn.KV_HEAD_MAJOR else (B, max_seq, Hkv, D)
-    kc0 = to_dev(normal(seed + 3, shape, oracle.F16), oracle.F16)
-    vc0 = to_dev(normal(seed + 4, shape, oracle.F16), oracle.F16)
+    kch, vch = normal(seed + 3, shape, dtype), normal(seed + 4, shape, dtype)
+    kc0, vc0 = to_dev(kch, dtype), to_dev(vch, dtype)
     lens_d = torch.tensor(lens, dtype=torch.int32, device="cuda")
-    qw = kw = None
+    qwh = kwh = qw = kw = None
     if norm:
-        qw = torch.from_numpy((0.5 * normal(seed + 5, (D,), oracle.F32)).astype(np.float32)).cuda()
-        kw = torch.from_numpy((0.5 * normal(seed + 6, (D,), oracle.F32)).astype(np.float32)).cuda()
-    scale = 1.0 / np.sqrt(D)
+        qwh = (0.5 * normal(seed + 5, (D,), oracle.F32)).astype(np.float32)
+        kwh = (0.5 * normal(seed + 6, (D,), oracle.F32)).astype(np.float32)
+        qw, kw = torch.from_numpy(qwh).cuda(), torch.from_numpy(kwh).cuda()
+    scale = float(np.float32(1.0 / np.sqrt(D)))
 
+    # the regular entry point on the same inputs
     ref = torch.empty(B, Hq, D, device="cuda")
     kc, vc = kc0.clone(), vc0.clone()
     b200attn.decode(ctx, q, kn, vn, kc, vc, lens_d, ref, scale, kv_layout=layout, rope_mode=rope, rope_theta=theta,
                     window=window, q_norm_w=qw, k_norm_w=kw)
     torch.cuda.synchronize()
+    # the CPU oracle
+    want, _, _ = oracle.decode(
+        qh, knh, vnh, kch, vch, np.asarray(lens, np.int32), B=B, Hq=Hq, Hkv=Hkv, D=D, max_seq=max_seq, scale=scale,
+        rope_theta=theta if rope != b200attn.ROPE_NONE else 0.0,
+        rope_mode=oracle.ROPE_GEMMA if rope == b200attn.ROPE_GEMMA else oracle.ROPE_DECODERONLY, window=window,
+        cache_layout=oracle.KV_HEAD_MAJOR if layout == b200attn.KV_HEAD_MAJOR else oracle.KV_POS_MAJOR,
+        cache_dtype=dtype, q_norm_w=qwh, k_norm_w=kwh, norm_eps=1e-6,
+        softmax_mode=oracle.SOFTMAX_GEMMA if rope == b200attn.ROPE_GEMMA else oracle.SOFTMAX_DECODERONLY)
 
     f = _noalloc_fn()
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    outs = []
     kc2, vc2 = kc0.clone(), vc0.clone()
-    for _ in range(2):  # two calls in a row share (and reuse) the static scratch
-        out = torch.full((B, Hq, D), float("nan"), device="cuda")
-        rc = f(oracle.F16, oracle.F16, oracle.F32, ptr(q), ptr(kn), ptr(vn), ptr(kc2), ptr(vc2), layout, ptr(lens_d),
+    outs = [torch.full((B, Hq, D), float("nan"), device="cuda") for _ in range(2)]
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    for out in outs:  # two calls in a row share (and reuse) the static scratch
+        rc = f(dtype, dtype, oracle.F32, ptr(q), ptr(kn), ptr(vn), ptr(kc2), ptr(vc2), layout, ptr(lens_d),
                B, Hq, Hkv, D, max_seq, scale, rope, theta, window, ptr(qw), ptr(kw), 1e-6, ptr(out), stream)
         assert rc == b200attn.B2A_OK, rc
-        torch.cuda.synchronize()
-        outs.append(to_np(out))
-    want = to_np(ref)
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before, f"device free memory changed by {free_before - free_after} bytes"
     for got in outs:
-        assert_close(got, want, what="no-alloc decode vs b2a_decode")
-    # the appended cache rows match too
+        assert_close(to_np(got), to_np(ref), what="no-alloc decode vs b2a_decode")
+        assert_close(to_np(got), want, what="no-alloc decode vs oracle")
+    # the first call appended the new rows; the second rewrote the same values
     assert torch.equal(kc2, kc) and torch.equal(vc2, vc)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _first_call_resolves_the_scratch():
+    """The first call on a device resolves the scratch array's address (which may load the module that
+    holds it); later calls allocate nothing.  Make that first call here, outside the measured calls."""
+    import torch
+    import b200attn
+    f = _noalloc_fn()
+    B, Hq, Hkv, D, S = 1, 2, 1, 64, 8
+    z = lambda *s: torch.zeros(*s, dtype=torch.float16, device="cuda")
+    q, kn, vn, kc, vc = z(B, Hq, D), z(B, Hkv, D), z(B, Hkv, D), z(B, Hkv, S, D), z(B, Hkv, S, D)
+    lens = torch.zeros(B, dtype=torch.int32, device="cuda")
+    out = torch.empty(B, Hq, D, device="cuda")
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    rc = f(oracle.F16, oracle.F16, oracle.F32, p(q), p(kn), p(vn), p(kc), p(vc), 0, p(lens), B, Hq, Hkv, D, S,
+           0.125, 0, 0.0, 0, None, None, 1e-6, p(out), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == b200attn.B2A_OK, rc
+    torch.cuda.synchronize()
 
 
 def test_noalloc_decode_matches_regular_decode_qwen_shape(ctx):
@@ -82,6 +114,16 @@ def test_noalloc_decode_matches_regular_decode_gemma_shape_long_context(ctx):
           rope=b200attn.ROPE_GEMMA, theta=1e6, window=0, norm=True, seed=911)
 
 
+@pytest.mark.parametrize("D", [64, 96, 128, 256])
+@pytest.mark.parametrize("dtype", [oracle.F16, oracle.BF16])
+def test_noalloc_decode_every_supported_head_dim_fits_this_gpu(ctx, D, dtype):
+    """The partial slots scale with the decode kernel's resident grid; on this GPU every supported head
+    dim and cache type must fit the static scratch and match the oracle."""
+    import b200attn
+    _case(ctx, B=3, Hq=8, Hkv=2, D=D, max_seq=2500, lens=[2400, 7, 1300], layout=b200attn.KV_POS_MAJOR,
+          rope=b200attn.ROPE_NEOX, theta=1e4, window=0, norm=False, seed=921 + D, dtype=dtype)
+
+
 def test_noalloc_decode_rejects_requests_beyond_the_scratch(ctx):
     import b200attn
     f = _noalloc_fn()
@@ -92,3 +134,15 @@ def test_noalloc_decode_rejects_requests_beyond_the_scratch(ctx):
     buf = ctypes.create_string_buffer(512)
     b200attn.lib().b2a_last_error(None, buf, 512)
     assert b"static scratch limit" in buf.value
+
+
+def test_noalloc_decode_rejects_negative_norm_eps(ctx):
+    import b200attn
+    f = _noalloc_fn()
+    dummy = ctypes.c_void_p(16)  # never dereferenced: the argument check fails first
+    rc = f(oracle.F16, oracle.F16, oracle.F32, dummy, dummy, dummy, dummy, dummy, 0, dummy,
+           2, 4, 1, 64, 128, 0.125, 0, 0.0, 0, dummy, dummy, -1.0, dummy, None)
+    assert rc == b200attn.B2A_EINVAL
+    buf = ctypes.create_string_buffer(512)
+    b200attn.lib().b2a_last_error(None, buf, 512)
+    assert b"norm_eps" in buf.value

@@ -308,10 +308,54 @@ def partition_units(unit_cost, n_ranks: int):
     return out
 
 
+_batch_local = threading.local()
+
+
+class GpuBatch:
+    """Submission coalescing, the mirror of DirectMlGpuBatch (WB/runtime/DirectMlGpuBatch.java):
+    outside a batch every CudaAttentionKernel.dispatch waits for its launch and checks the
+    device status (as DirectMlAttentionKernel.dispatch waits on a fence through
+    D3D12Bindings.executeAndWait); inside one, dispatches return at once and close()
+    synchronises once and raises the first device failure (B2A_ETIMEOUT, B2A_EDEVICE).
+    Thread-bound and re-entrant: a nested begin() shares the outer batch and only the
+    outermost close() drains."""
+
+    def __init__(self, ctx: "Context", stream=None):
+        self.ctx, self.stream, self._outer = ctx, stream, None
+
+    @classmethod
+    def begin(cls, ctx: "Context", stream=None) -> "GpuBatch":
+        b = cls(ctx, stream)
+        b._outer = getattr(_batch_local, "current", None)
+        if b._outer is None:
+            _batch_local.current = b
+        return b
+
+    @staticmethod
+    def current():
+        return getattr(_batch_local, "current", None)
+
+    def close(self):
+        if self._outer is not None:
+            return  # nested: the outermost batch drains
+        if getattr(_batch_local, "current", None) is self:
+            _batch_local.current = None
+            self.ctx.check_device_status(self.stream)
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
 class CudaAttentionKernel:
     """AttentionKernel for the CUDA backend, shaped like DirectMlAttentionKernel:
     fixed (B, H, S, D, scale, hasMask) at construction, dispatch(q, k, v, mask, y, scale).
-    Unlike the DirectML kernel it keeps no [B,H,S,S] intermediates."""
+    Unlike the DirectML kernel it keeps no [B,H,S,S] intermediates.  A dispatch outside a
+    GpuBatch waits for the launch and raises B200RuntimeException if the device flagged a
+    failure (a bounded wait that ran out: B2A_ETIMEOUT), so it never returns with undefined
+    output; inside a batch the check happens when the batch closes."""
 
     def __init__(self, ctx: Context, batch: int, heads: int, seq: int, head_dim: int, scale: float, has_mask: bool):
         if batch <= 0 or heads <= 0 or seq <= 0 or head_dim <= 0:
@@ -335,9 +379,13 @@ class CudaAttentionKernel:
                     f"got {t.numel()}")
         if self.has_mask and mask is None:
             raise B200RuntimeException("kernel was built with hasMask=true but mask=null")
+        if not self.has_mask and mask is not None:
+            raise B200RuntimeException("kernel was built with hasMask=false but mask!=null")
         shape = (self.B, self.H, self.S, self.D)
         mha(self.ctx, q.view(shape), k.view(shape), v.view(shape), y.view(shape), scale,
             mask=mask if self.has_mask else None, layout=HEAD_MAJOR, stream=stream)
+        if GpuBatch.current() is None:  # executeAndWait: wait and surface device failures now
+            self.ctx.check_device_status(stream)
 
     def close(self):
         self.closed = True

@@ -25,6 +25,7 @@ struct b2a_context {
     std::string last_error;
     size_t ws_limit = 0;  // 0: unlimited
     int* status = nullptr;  // device int[kStatusBufferInts]: error flags, prefill work-item counters
+    int* status_host = nullptr;  // pinned int[kStatusWords]: where b2a_check_device_status reads the flags
     // decode workspace: [counters][partials]
     void* dec_ws = nullptr;
     size_t dec_ws_bytes = 0;
@@ -269,9 +270,13 @@ B2A_API int b2a_create(int device, b2a_context** out) {
     ctx->sm_count = prop.multiProcessorCount;
     e = cudaMalloc(&ctx->status, kStatusBufferInts * sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(ctx->status, 0, kStatusBufferInts * sizeof(int));
+    if (e == cudaSuccess) e = cudaMallocHost(&ctx->status_host, kStatusWords * sizeof(int));
     if (e != cudaSuccess) {
+        if (ctx->status) cudaFree(ctx->status);
         delete ctx;
-        return fail(nullptr, B2A_ECUDA, "status buffer: %s", cudaGetErrorString(e));
+        cudaGetLastError();
+        return fail(nullptr, e == cudaErrorMemoryAllocation ? B2A_EOOM : B2A_ECUDA, "status buffer: %s",
+                    cudaGetErrorString(e));
     }
     *out = ctx;
     return B2A_OK;
@@ -282,6 +287,7 @@ B2A_API int b2a_destroy(b2a_context* ctx) {
     {
         DeviceGuard guard(ctx->device);
         if (ctx->status) cudaFree(ctx->status);
+        if (ctx->status_host) cudaFreeHost(ctx->status_host);
         if (ctx->dec_ws) cudaFree(ctx->dec_ws);
         if (ctx->pf_ws) cudaFree(ctx->pf_ws);
         if (ctx->split_ws) cudaFree(ctx->split_ws);
@@ -341,19 +347,23 @@ B2A_API int b2a_check_device_status(b2a_context* ctx, void* stream) {
     if (!ctx) return B2A_EINVAL;
     DeviceGuard guard(ctx->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaStreamSynchronize(s);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "stream synchronize");
-    int st[kStatusWords] = {0, 0, 0, 0};
-    e = cudaMemcpy(st, ctx->status, sizeof(st), cudaMemcpyDeviceToHost);
+    // one stream-ordered copy of the flags into pinned memory, one synchronisation
+    cudaError_t e = cudaMemcpyAsync(ctx->status_host, ctx->status, kStatusWords * sizeof(int),
+                                    cudaMemcpyDeviceToHost, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "status read");
-    if (st[0] == 0) return B2A_OK;
-    cudaMemset(ctx->status, 0, sizeof(st));
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "stream synchronize");
+    const int flags = ctx->status_host[0];
+    if (flags == 0) return B2A_OK;
+    e = cudaMemsetAsync(ctx->status, 0, kStatusWords * sizeof(int), s);  // ordered before later launches
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "status clear");
     std::string msg;
-    if (st[0] & 1) msg += "a ctx_lens entry was outside [0, max_seq); its outputs are NaN. ";
-    if (st[0] & 2) msg += "decode work items exceeded the workspace capacity. ";
-    if (st[0] & 4) msg += "a bf16 input exceeded the fp16 operand range (|x| > 65504). ";
-    if (st[0] & 8) msg += "a bounded device wait ran out (attention pipeline aborted). ";
-    return fail(ctx, B2A_EDEVICE, "%s", msg.c_str());
+    if (flags & 8) msg += "a bounded device wait ran out (attention pipeline aborted; its outputs are undefined). ";
+    if (flags & 1) msg += "a ctx_lens entry was outside [0, max_seq); its outputs are NaN. ";
+    if (flags & 2) msg += "decode work items exceeded the workspace capacity. ";
+    if (flags & 4) msg += "a bf16 input exceeded the fp16 operand range (|x| > 65504). ";
+    // a timed-out pipeline is reported as such; the other flags are failed device-side argument checks
+    return fail(ctx, (flags & 8) ? B2A_ETIMEOUT : B2A_EDEVICE, "%s", msg.c_str());
 }
 
 // ----------------------------------------------------------------- encoder

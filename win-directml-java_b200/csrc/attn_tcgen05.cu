@@ -143,8 +143,10 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: false when kWaitNs elapse (status bit 3) or another role /
-// another CTA already aborted.
+// Bounded wait: false when kWaitNs elapse or another role / another CTA of this launch
+// already aborted.  A timeout raises status bit 3 (the sticky report b2a_check_device_status
+// reads) and the launch's abort word (status[kStatusAbortWord]), which the other CTAs poll;
+// the abort word is reset by the launch's last CTA, so later launches run normally.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status) {
     if (mbar_test(bar, parity)) return true;
     const uint64_t t0 = global_ns();
@@ -152,13 +154,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
         if (mbar_test(bar, parity)) return true;
         if ((i & 1023u) == 0) {
             if (*abort_flag) return false;
-            if (*(volatile int*)status & 8) {
+            if (*(volatile int*)(status + kStatusAbortWord)) {
                 *abort_flag = 1;
                 return false;
             }
             if (global_ns() - t0 > kWaitNs) {
                 *abort_flag = 1;
                 atomicOr(status, 8);
+                atomicExch(status + kStatusAbortWord, 1);
                 return false;
             }
         }
@@ -864,14 +867,16 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
-    // the last CTA to finish resets the work-item counters for the next launch: every CTA
-    // has fetched its last item (its producer is past the barrier above) before it counts
+    // the last CTA to finish resets the work-item counters and the abort word for the next
+    // launch: every CTA has fetched its last item and passed its last wait (its roles are past
+    // the barrier above) before it counts
     if (tid == 0) {
         int* const sched = p.sched;
         __threadfence();
         if (atomicAdd(sched + 1, 1) == (int)gridDim.x - 1) {
             atomicExch(sched, 0);
             atomicExch(sched + 1, 0);
+            atomicExch(status + kStatusAbortWord, 0);
         }
     }
 }

@@ -92,6 +92,7 @@ extern "C" B2A_API int b2a_decode_noalloc(int q_dtype, int cache_dtype, int out_
     if ((q_norm_w == nullptr) != (k_norm_w == nullptr))
         return reject(B2A_EINVAL, "q_norm_w and k_norm_w must be given together");
     if (!(scale > 0.f)) return reject(B2A_EINVAL, "scale must be a positive number");
+    if (q_norm_w && !(norm_eps >= 0.f)) return reject(B2A_EINVAL, "norm_eps must not be negative");
     // only the tensor-core decode (16-bit caches, head_dim 64/96/128/256) uses scratch
     if (!decode_tc_supported(D, cache_dtype))
         return reject(B2A_ENOTSUP, "b2a_decode_noalloc needs an fp16/bf16 cache and head_dim 64, 96, 128 or 256 "

@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         // microseconds, and issued one after another they were most of a piece's fixed cost.
         const bool rope = p.append && p.rope_mode != 0;
         double inv_f = 0.0;
-        if (rope && tid < D / 2) inv_f = __ldg(p.inv_freq + tid);
+        if (rope && tid < D / 2) inv_f = p.inv_freq[tid];  // a kernel-parameter array: plain load
         constexpr int kHeadsPerWarp = kHeads / kWarps;
         static_assert(kHeads % kWarps == 0 && D / 2 <= kThreads, "prologue work split");
         HeadLoad<D> qload[kHeadsPerWarp];

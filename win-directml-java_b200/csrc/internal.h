@@ -109,10 +109,14 @@ int attn_simt_split_plan(const AttnParams& p, int sm_count, size_t* part_bytes, 
 cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t stream, const SimtSplit* split = nullptr);
 // The context's device status buffer: words [0, kStatusWords) are the error flags
 // b2a_check_device_status reports and clears; words kStatusSchedWord and the next one are
-// the persistent prefill kernel's work-item counters (zero between launches: the last CTA
-// of each launch resets them).
+// the persistent prefill kernel's work-item counters, and word kStatusAbortWord its
+// per-launch abort word (a CTA whose bounded wait ran out sets it so that the launch's other
+// CTAs stop too).  All three are zero between launches: the last CTA of each launch resets
+// them, so one timed-out launch does not abort the next ones (the sticky report stays in
+// the error flags until they are read).
 constexpr int kStatusWords = 4;
 constexpr int kStatusSchedWord = 4;
+constexpr int kStatusAbortWord = 6;
 constexpr int kStatusBufferInts = 8;
 
 // tcgen05 / TMEM / TMA kernel (fp16 operands, head_dim 64, 96, 128); status bit 3 = bounded wait ran out.
