@@ -117,6 +117,7 @@ def test_encoder_minilm_config_full_size(ctx, layout):
     """configs[1] at full size: B=64, S=128, H=12, D=32, fp16, key lengths ~ U[16,128]."""
     lens = oracle.splitmix_uniform_int(2, 64, 16, 128)
     got, want = _encoder_case(ctx, B=64, H=12, S=128, D=32, dtype=oracle.F16, lens=lens, layout=layout, seed=200)
+    assert ctx.last_attention_kernel() == "tcgen05"  # head dim 32 runs on the tensor-core kernel
     assert_close(got, want, what="minilm encoder")
 
 

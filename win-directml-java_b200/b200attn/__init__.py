@@ -94,6 +94,8 @@ def lib() -> ctypes.CDLL:
         L.b2a_reserve_decode.argtypes = [_vp, _i, _i, _i, _i]
         L.b2a_check_device_status.argtypes = [_vp, _vp]
         L.b2a_test_inject_wait_timeout.argtypes = [_vp]
+        L.b2a_test_last_attention_kernel.argtypes = [_vp]
+        L.b2a_test_last_attention_kernel.restype = _i
         L.b2a_mha.argtypes = [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _i, _vp]
         L.b2a_prefill_causal.argtypes = [_vp, _i, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _d, _i, _i,
                                          _vp, _vp]
@@ -197,6 +199,11 @@ class Context:
 
     def check_device_status(self, stream=None):
         self.check(lib().b2a_check_device_status(self._h, _stream(stream)))
+
+    def last_attention_kernel(self) -> str:
+        """Test hook (include/b200attn_testing.h): the kernel family of the last whole-sequence
+        attention launch: "tcgen05", "warp_mma", "generic" or "" before any."""
+        return {1: "tcgen05", 2: "warp_mma", 3: "generic"}.get(lib().b2a_test_last_attention_kernel(self._h), "")
 
     def inject_wait_timeout(self):
         """Test hook (include/b200attn_testing.h): the next tcgen05 attention launch of this

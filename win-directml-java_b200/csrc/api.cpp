@@ -43,6 +43,9 @@ struct b2a_context {
     // test hook (b2a_test_inject_wait_timeout): the next tcgen05 attention launch
     // leaves one K/V copy unissued
     bool inject_wait_timeout = false;
+    // test hook (b2a_test_last_attention_kernel): the kernel the last whole-sequence
+    // attention launch took
+    int last_attention_kernel = 0;
 };
 
 namespace {
@@ -151,9 +154,14 @@ cudaError_t launch_attention(b2a_context* ctx, const AttnParams& p, cudaStream_t
     if (attn_tcgen05_supported(p)) {
         const bool stall = ctx->inject_wait_timeout;
         ctx->inject_wait_timeout = false;
+        ctx->last_attention_kernel = B2A_TEST_KERNEL_TCGEN05;
         return launch_attn_tcgen05(p, ctx->status, s, stall);
     }
-    if (attn_tc_supported(p)) return launch_attn_tc(p, s);
+    if (attn_tc_supported(p)) {
+        ctx->last_attention_kernel = B2A_TEST_KERNEL_WARP_MMA;
+        return launch_attn_tc(p, s);
+    }
+    ctx->last_attention_kernel = B2A_TEST_KERNEL_GENERIC;
     // generic kernel: launches too small to fill the GPU split each query block's keys
     // over several CTAs; without room for the split workspace they run unsplit
     size_t part_bytes = 0, counter_ints = 0;
@@ -341,6 +349,10 @@ B2A_API int b2a_test_inject_wait_timeout(b2a_context* ctx) {
     if (!ctx) return B2A_EINVAL;
     ctx->inject_wait_timeout = true;
     return B2A_OK;
+}
+
+B2A_API int b2a_test_last_attention_kernel(const b2a_context* ctx) {
+    return ctx ? ctx->last_attention_kernel : 0;
 }
 
 B2A_API int b2a_check_device_status(b2a_context* ctx, void* stream) {

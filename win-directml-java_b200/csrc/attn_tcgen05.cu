@@ -38,6 +38,10 @@
 // waits (bounded) for its own TMA copies, the MMA thread drains its MMAs,
 // TMEM is freed and the CTA returns.
 //
+// Head dims 32, 64, 96, 128 and 256.  A K/V/Q row is staged as 64-element panels
+// (the TMA box is 64 wide; dims past D are zero-filled): at D = 32 the QK MMAs read
+// the first two 16-element K steps of each row and the PV MMAs have N = 32, so the
+// zero half of the panel is never read.
 // Same semantics as attn_simt.cu / attn_mma.cu (the reference citations are
 // there); operands are fp16 (bf16 callers are converted by the host layer).
 // The additive [B][S] key mask has its own instantiation (kAdditive).
@@ -1007,7 +1011,7 @@ cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream, b
 bool attn_tcgen05_supported(const AttnParams& p) {
     // fp16 operands only: P goes to TMEM as fp16 and both MMA operands share one type
     if (p.in_dtype != kF16) return false;
-    if (!(p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256)) return false;
+    if (!(p.D == 32 || p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256)) return false;
     const int64_t strides[] = {p.q_sb, p.q_ss, p.q_sh, p.k_sb, p.k_ss, p.k_sh};
     for (int64_t s : strides)
         if (s % 8 != 0 || s <= 0) return false;
@@ -1016,14 +1020,17 @@ bool attn_tcgen05_supported(const AttnParams& p) {
         if (x % 16 != 0) return false;
     // the work-item counter reaches items + grid within int32
     if (p.Hq > 65535 || p.B > 65535 || work_items(p) > INT32_MAX / 2 || encode_fn() == nullptr) return false;
-    const cudaError_t ready = p.D == 64 ? kernel_ready_for<64>(p) : p.D == 96 ? kernel_ready_for<96>(p)
-                                                                               : p.D == 128 ? kernel_ready_for<128>(p)
-                                                                                            : kernel_ready_for<256>(p);
+    const cudaError_t ready = p.D == 32    ? kernel_ready_for<32>(p)
+                              : p.D == 64  ? kernel_ready_for<64>(p)
+                              : p.D == 96  ? kernel_ready_for<96>(p)
+                              : p.D == 128 ? kernel_ready_for<128>(p)
+                                           : kernel_ready_for<256>(p);
     return ready == cudaSuccess;
 }
 
 cudaError_t launch_attn_tcgen05(const AttnParams& p, int* status, cudaStream_t stream, bool stall) {
     switch (p.D) {
+        case 32: return launch_impl<32>(p, status, stream, stall);
         case 64: return launch_impl<64>(p, status, stream, stall);
         case 96: return launch_impl<96>(p, status, stream, stall);
         case 128: return launch_impl<128>(p, status, stream, stall);
