@@ -202,12 +202,21 @@ class DecodeWorkload:
         if batch > 0:  # smaller batch for profiler captures only
             self.B = batch
         from b200attn import synthetic
-        # one global batch of world * B sequences; each rank takes its cost-balanced,
-        # equal-count shard (b200attn.sharding.plan_shards; cost = keys attended)
+        # One global batch of world * B sequences.  The partition unit is (sequence, kv head):
+        # each rank takes a cost-balanced, equal-count shard of the units (plan_shards; cost =
+        # keys attended) and runs them as sequences with one kv head and Hq/Hkv q heads.  With
+        # one kv head (c5) a unit is a sequence.  The outputs are reassembled in the e2e arm.
+        self.world, self.rank = world, rank
+        self.seqs_per_rank = self.B
+        self.Hkv_model, self.Hq_model = self.Hkv, self.Hq
         lens_all = synthetic.uniform_int(seed, self.B * world, self.lo, self.hi)
+        self.plan = None
         if world > 1:
             from b200attn import sharding
-            self.lens = np.ascontiguousarray(lens_all[sharding.plan_shards(lens_all.astype(np.int64) + 1, world)[rank]])
+            unit_lens = np.repeat(lens_all, self.Hkv)  # unit u = (sequence u // Hkv, kv head u % Hkv)
+            self.plan = sharding.plan_shards(unit_lens.astype(np.int64) + 1, world)
+            self.lens = np.ascontiguousarray(unit_lens[self.plan[rank]])
+            self.B, self.Hq, self.Hkv = len(self.lens), self.Hq // self.Hkv, 1
         else:
             self.lens = lens_all
         self.max_seq = self.hi + 1
@@ -238,9 +247,11 @@ class DecodeWorkload:
         self.h_vn = [pin(t) for t in self.vn]
         self.h_lens = pin(self.lens_d)
         self.h_out = [torch.empty(B, Hq, D).pin_memory() for _ in self.layers]
+        if world > 1:  # every rank receives the whole batch's outputs of both layers
+            self.h_out_all = torch.empty(len(self.layers), B * world, Hq, D).pin_memory()
 
     def tokens_per_step(self):
-        return self.B
+        return self.seqs_per_rank
 
     def kernel_launches_per_step(self):
         return len(self.layers)
@@ -282,15 +293,31 @@ class DecodeWorkload:
             self.kn[i].copy_(self.h_kn[i], non_blocking=True)
             self.vn[i].copy_(self.h_vn[i], non_blocking=True)
             self.launch(ctx, i, stream)
-            self.h_out[i].copy_(self.out[i], non_blocking=True)
+            if self.world == 1:
+                self.h_out[i].copy_(self.out[i], non_blocking=True)
+        if self.world > 1:
+            # output reassembly: one NCCL all-gather of the equal shards (both layers at once),
+            # scattered back into unit order, then the whole batch's outputs to the host
+            from b200attn import sharding
+            local = self.torch.stack(self.out, dim=1)  # [units, layers, G, D]
+            full = sharding.gather_shards(local, self.plan)
+            self.h_out_all.copy_(full.transpose(0, 1), non_blocking=True)
 
     def e2e_bytes(self):
         h2d = self.lens.nbytes + sum(t.numel() * t.element_size() for t in self.h_q + self.h_kn + self.h_vn)
-        d2h = sum(t.numel() * t.element_size() for t in self.h_out)
+        if self.world > 1:
+            d2h = self.h_out_all.numel() * self.h_out_all.element_size()
+        else:
+            d2h = sum(t.numel() * t.element_size() for t in self.h_out)
         return h2d, d2h
 
     def config(self):
-        return decode_config(self.name, self.B, self.lens, self.max_seq)
+        cfg = decode_config(self.name, self.seqs_per_rank, self.lens, self.max_seq)
+        if self.world > 1:
+            cfg["partition_unit"] = "(sequence, kv head)" if self.Hkv_model > 1 else "sequence"
+            cfg["units_per_rank"] = self.B
+            cfg["reassembly"] = "NCCL all_gather of equal shards in the e2e arm (b200attn.sharding.gather_shards)"
+        return cfg
 
 
 class PrefillWorkload:

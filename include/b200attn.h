@@ -49,7 +49,7 @@ typedef enum b2a_status {
     B2A_OK = 0,
     B2A_EINVAL = 1,   /* bad shape, dtype, head divisibility, null or misaligned pointer */
     B2A_ECUDA = 2,    /* a CUDA runtime call failed */
-    B2A_ENCCL = 3,    /* reserved for collective failures */
+    B2A_ENCCL = 3,    /* NCCL failed or could not be loaded (b2a_group_*, b2a_sharded_*) */
     B2A_ETIMEOUT = 4, /* a bounded device-side wait ran out (b2a_check_device_status) */
     B2A_EOOM = 5,     /* device allocation failed or exceeded the context's cap */
     B2A_ENOTSUP = 6,  /* valid arguments, but no kernel for this combination */
@@ -304,6 +304,49 @@ B2A_API int b2a_gemma_fused_attention_context(b2a_context* ctx, const float* q, 
                                               int first_valid, int query_pos, float scale, void* stream);
 
 /* ------------------------------------------------------------ multi-GPU */
+
+/* One process driving several GPUs of a node: the multi-device counterpart of
+ * b2a_create (the reference's DirectMlContextImpl is single-device and the
+ * reference has no multi-GPU path).  A group holds one context per device and an NCCL
+ * communicator clique (ncclCommInitAll).  NCCL is loaded at run time
+ * (libnccl.so.2, or the file named by the B2A_NCCL_LIBRARY environment variable);
+ * a missing library and every NCCL failure -- a rank count below 1 or a device
+ * list NCCL rejects included -- return B2A_ENCCL.  Not thread-safe. */
+typedef struct b2a_group b2a_group;
+B2A_API int b2a_group_create(int ndev, const int* devices, b2a_group** out);
+B2A_API int b2a_group_destroy(b2a_group* g);
+/* Message of the group's last failure (g may be NULL for b2a_group_create). */
+B2A_API int b2a_group_last_error(const b2a_group* g, char* buf, size_t n);
+B2A_API int b2a_group_size(const b2a_group* g);
+/* The context of rank `rank` (owned by the group; do not destroy it). */
+B2A_API int b2a_group_context(b2a_group* g, int rank, b2a_context** ctx);
+/* b2a_check_device_status on every rank (streams[r] or the default stream). */
+B2A_API int b2a_group_check_device_status(b2a_group* g, void* const* streams);
+
+/* Sharded decode: every argument that is a tensor is a per-rank array of device
+ * pointers (index r = rank r, memory on that rank's device); each rank holds an
+ * equal shard of B_shard sequences and runs b2a_decode on it (same argument
+ * meaning), then one grouped ncclAllGather copies every rank's o_shard
+ * [B_shard, Hq, D] into o_gathered[r] [n_ranks * B_shard, Hq, D] on every rank,
+ * rank-major.  Partitioning by (sequence, kv head): pass each unit as a sequence
+ * with Hkv = 1 and Hq = Hq/Hkv (its cache rows and q heads), as planned by
+ * b2a_partition_units.  streams: per-rank cudaStream_t array or NULL.
+ * Asynchronous; a rank's argument failure returns its status with the rank named. */
+B2A_API int b2a_sharded_decode(b2a_group* g, int q_dtype, int cache_dtype, int out_dtype,
+                               const void* const* q_new, const void* const* k_new, const void* const* v_new,
+                               void* const* k_cache, void* const* v_cache, int kv_layout,
+                               const int32_t* const* ctx_lens, int B_shard, int Hq, int Hkv, int D, int max_seq,
+                               float scale, int rope_mode, double rope_theta, int window,
+                               const float* const* q_norm_w, const float* const* k_norm_w, float norm_eps,
+                               void* const* o_shard, void* const* o_gathered, void* const* streams);
+
+/* Sharded encoder attention: b2a_mha on every rank's B_shard sequences (per-rank
+ * pointer arrays; mask / key_lengths arrays may be NULL), then one grouped
+ * ncclAllGather of y_shard into y_gathered[r] (rank-major along the batch). */
+B2A_API int b2a_sharded_mha(b2a_group* g, int in_dtype, int out_dtype, const void* const* q, const void* const* k,
+                            const void* const* v, const float* const* mask, const int32_t* const* key_lengths,
+                            void* const* y_shard, void* const* y_gathered, int B_shard, int H, int S, int D,
+                            float scale, int layout, void* const* streams);
 
 /* Partition `n_units` independent (sequence, kv-head) units over `n_ranks`
  * ranks with equal unit counts (n_units % n_ranks == 0 required), balancing

@@ -55,3 +55,21 @@ def test_partition_units_equal_counts_and_balance():
 def test_partition_units_rejects_uneven_split():
     with pytest.raises(ValueError):
         b200attn.partition_units(np.ones(10, np.int64), 4)
+
+
+def test_group_without_an_nccl_library_is_b2a_enccl(monkeypatch):
+    """The multi-GPU group loads NCCL at run time; a missing library is an NCCL failure (B2A_ENCCL)
+    reported before any device is touched."""
+    monkeypatch.setenv("B2A_NCCL_LIBRARY", "/nonexistent/libnccl.so.2")
+    with pytest.raises(b200attn.B200RuntimeException) as ei:
+        b200attn.Group([0])
+    assert ei.value.status == b200attn.B2A_ENCCL
+    assert "NCCL could not be loaded" in str(ei.value)
+
+
+def test_group_with_a_bad_rank_count_is_b2a_enccl():
+    """A clique of zero ranks is rejected by NCCL's own argument check (no device is touched)."""
+    with pytest.raises(b200attn.B200RuntimeException) as ei:
+        b200attn.Group([])
+    assert ei.value.status == b200attn.B2A_ENCCL
+    assert "ncclCommInitAll(0 ranks)" in str(ei.value)

@@ -129,6 +129,18 @@ def test_encoder_ragged_length_tensor_core_dims(ctx, layout, D):
     assert_close(got, want, what=f"encoder D={D}")
 
 
+@pytest.mark.parametrize("layout,D,S", [(0, 32, 128), (1, 64, 100), (1, 96, 77), (0, 128, 128)])
+def test_encoder_short_sequences_two_heads_per_work_item(ctx, layout, D, S):
+    """Bidirectional sequences of at most 128 keys take two (batch, head) pairs per tcgen05 work item
+    (one per softmax group): an odd pair count leaves the last item with one tile, pairs straddle batch
+    boundaries, and a sequence without valid keys (length 0) sits in either tile of an item."""
+    B, H = 3, 3
+    got, want = _encoder_case(ctx, B=B, H=H, S=S, D=D, dtype=oracle.F16, lens=[S, 0, 37], layout=layout,
+                              seed=800 + D)
+    assert ctx.last_attention_kernel() == "tcgen05"
+    assert_close(got, want, what=f"packed encoder D={D} S={S}")
+
+
 def test_encoder_zero_and_full_lengths(ctx):
     # a text with no valid key averages V (softmax of equal -1e9 scores), as the reference does
     got, want = _encoder_case(ctx, B=3, H=2, S=64, D=32, dtype=oracle.F16, lens=[0, 64, 1], layout=1, seed=300)
@@ -181,6 +193,7 @@ def test_encoder_additive_mask_fp16(ctx):
     b200attn.mha(ctx, to_dev(q, oracle.F16), to_dev(k, oracle.F16), to_dev(v, oracle.F16), y, scale,
                  mask=torch.from_numpy(mask).cuda())
     torch.cuda.synchronize()
+    assert ctx.last_attention_kernel() == "tcgen05"  # 12 heads of 96 keys: packed work items, additive mask
     assert_close(to_np(y), want, what="additive mask")
 
 

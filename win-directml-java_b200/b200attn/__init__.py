@@ -108,10 +108,21 @@ def lib() -> ctypes.CDLL:
                                         _vp, _f, _vp, _vp]
         L.b2a_gemma_fused_attention_context.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp]
         L.b2a_partition_units.argtypes = [_i, _i, _vp, _vp]
+        L.b2a_group_create.argtypes = [_i, _vp, ctypes.POINTER(_vp)]
+        L.b2a_group_destroy.argtypes = [_vp]
+        L.b2a_group_last_error.argtypes = [_vp, ctypes.c_char_p, ctypes.c_size_t]
+        L.b2a_group_size.argtypes = [_vp]
+        L.b2a_group_context.argtypes = [_vp, _i, ctypes.POINTER(_vp)]
+        L.b2a_group_check_device_status.argtypes = [_vp, _vp]
+        L.b2a_sharded_decode.argtypes = [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _f, _i,
+                                         _d, _i, _vp, _vp, _f, _vp, _vp, _vp]
+        L.b2a_sharded_mha.argtypes = [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _i, _vp]
         for name in ("b2a_create", "b2a_destroy", "b2a_last_error", "b2a_set_workspace_limit", "b2a_workspace_bytes",
                      "b2a_reserve_decode", "b2a_check_device_status", "b2a_mha", "b2a_prefill_causal", "b2a_decode",
                      "b2a_qwen_rope_and_append", "b2a_qwen_gqa_attention_decode", "b2a_qwen_decode_step", "b2a_prefill_gemma",
-                     "b2a_gemma_fused_attention_context", "b2a_partition_units", "b2a_test_inject_wait_timeout"):
+                     "b2a_gemma_fused_attention_context", "b2a_partition_units", "b2a_test_inject_wait_timeout",
+                     "b2a_group_create", "b2a_group_destroy", "b2a_group_last_error", "b2a_group_size",
+                     "b2a_group_context", "b2a_group_check_device_status", "b2a_sharded_decode", "b2a_sharded_mha"):
             getattr(L, name).restype = _i
         _lib = L
         return _lib
@@ -302,6 +313,100 @@ def decode(ctx: Context, q_new, k_new, v_new, k_cache, v_cache, ctx_lens, o, sca
                                Hkv, D, max_seq, scale, rope_mode, rope_theta, window, _ptr(q_norm_w), _ptr(k_norm_w),
                                norm_eps, _ptr(o), _stream(stream)))
     return o
+
+
+def _ptr_array(tensors):
+    """A C array of device pointers (None -> NULL entry) kept alive by the caller."""
+    arr = (ctypes.c_void_p * len(tensors))()
+    for i, t in enumerate(tensors):
+        arr[i] = None if t is None else _ptr(t).value
+    return arr
+
+
+class Group:
+    """Several GPUs driven from one process: one Context per device and an NCCL clique
+    (b2a_group_create).  The sharded calls run each rank's equal shard on its own device
+    and reassemble the outputs with one grouped ncclAllGather."""
+
+    def __init__(self, devices):
+        devs = (ctypes.c_int * len(devices))(*devices)
+        self._h = _vp()
+        rc = lib().b2a_group_create(len(devices), devs, ctypes.byref(self._h))
+        if rc != B2A_OK:
+            raise _error(rc, self._message(None))
+        self.devices = list(devices)
+
+    @staticmethod
+    def _message(h) -> str:
+        buf = ctypes.create_string_buffer(2048)
+        lib().b2a_group_last_error(h, buf, len(buf))
+        return buf.value.decode(errors="replace")
+
+    def check(self, rc: int):
+        if rc != B2A_OK:
+            raise _error(rc, self._message(self._h))
+
+    def size(self) -> int:
+        return lib().b2a_group_size(self._h)
+
+    def close(self):
+        if self._h:
+            lib().b2a_group_destroy(self._h)
+            self._h = _vp()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _streams(self, streams):
+        import torch
+        if streams is None:
+            streams = [torch.cuda.current_stream(d) for d in self.devices]
+        arr = (ctypes.c_void_p * len(streams))()
+        for i, s in enumerate(streams):
+            arr[i] = s.cuda_stream
+        return arr
+
+    def check_device_status(self, streams=None):
+        self.check(lib().b2a_group_check_device_status(self._h, self._streams(streams)))
+
+    def decode(self, q_new, k_new, v_new, k_cache, v_cache, ctx_lens, o_shard, o_gathered, scale: float, *,
+               kv_layout: int = KV_HEAD_MAJOR, rope_mode: int = ROPE_NEOX, rope_theta: float = 10000.0,
+               window: int = 0, q_norm_w=None, k_norm_w=None, norm_eps: float = 1e-6, streams=None):
+        """Per-rank lists of tensors (rank r's on device r): b2a_decode of every shard, then
+        o_gathered[r] = concatenation of all ranks' o_shard (rank-major)."""
+        B, Hq, D = q_new[0].shape
+        Hkv = k_new[0].shape[1]
+        max_seq = k_cache[0].shape[2] if kv_layout == KV_HEAD_MAJOR else k_cache[0].shape[1]
+        keep = [_ptr_array(x) for x in (q_new, k_new, v_new, k_cache, v_cache, ctx_lens, o_shard, o_gathered)]
+        qw = _ptr_array(q_norm_w) if q_norm_w is not None else None
+        kw = _ptr_array(k_norm_w) if k_norm_w is not None else None
+        self.check(lib().b2a_sharded_decode(
+            self._h, _dtype_code(q_new[0]), _dtype_code(k_cache[0]), _dtype_code(o_shard[0]), *keep[:5], kv_layout,
+            keep[5], B, Hq, Hkv, D, max_seq, scale, rope_mode, rope_theta, window, qw, kw, norm_eps, keep[6], keep[7],
+            self._streams(streams)))
+
+    def mha(self, q, k, v, y_shard, y_gathered, scale: float, *, mask=None, key_lengths=None,
+            layout: int = HEAD_MAJOR, streams=None):
+        """Per-rank lists: b2a_mha of every shard, then y_gathered[r] = all ranks' y_shard (batch-major)."""
+        if layout == HEAD_MAJOR:
+            B, H, S, D = q[0].shape
+        else:
+            B, S, H, D = q[0].shape
+        keep = [_ptr_array(x) for x in (q, k, v)]
+        m = _ptr_array(mask) if mask is not None else None
+        kl = _ptr_array(key_lengths) if key_lengths is not None else None
+        self.check(lib().b2a_sharded_mha(self._h, _dtype_code(q[0]), _dtype_code(y_shard[0]), *keep, m, kl,
+                                         _ptr_array(y_shard), _ptr_array(y_gathered), B, H, S, D, scale, layout,
+                                         self._streams(streams)))
 
 
 def partition_units(unit_cost, n_ranks: int):

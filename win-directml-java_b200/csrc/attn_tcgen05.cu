@@ -96,8 +96,11 @@ struct TcParams {
     int* status;
     int fmt;  // 0 = fp16, 1 = bf16 operands
     int* sched;   // device int[2]: next work item, CTAs finished (zero between launches)
-    int n_items;  // work items: query-tile pairs x heads x batch
+    int n_items;  // work items: query-tile pairs x heads x batch (packed: ceil(heads x batch / 2))
     int stall;    // test hook: CTA 0 does not issue ring item 1 (its first item's V(0), K(1))
+    // packed items (bidirectional, S <= 128, two query tiles per item): tile A and tile B are the
+    // single query tiles of two consecutive (batch, head) pairs, so both softmax groups work
+    int packed;
 };
 
 template <int D>
@@ -110,8 +113,12 @@ struct TcGeo {
     static constexpr uint32_t kOcol = 128u * kTiles;  // first O column (the S tiles come first)
     // ring stages; at D = 256 one (a step's softmax + 24 MMAs outlast the next tiles' loads)
     static constexpr int kStages = D <= 64 ? 3 : (D <= 128 ? 2 : 1);
-    static constexpr int oQ = 0;                   // Q_A (, Q_B)
-    static constexpr int oK = kTiles * kTileBytes;
+    // Q buffers per tile: two at D <= 64, so that the next work item's Q tiles load while the
+    // current item still reads its own (short items would otherwise wait for Q after every item)
+    static constexpr int kQBuf = D <= 64 ? 2 : 1;
+    static constexpr int kQTiles = kQBuf * kTiles;
+    static constexpr int oQ = 0;                   // Q tiles: buffer-major, tile-minor
+    static constexpr int oK = kQTiles * kTileBytes;
     static constexpr int oV = oK + kStages * kTileBytes;
     static constexpr int oBar = oV + kStages * kTileBytes;
     static constexpr int kBytes = oBar + 512;  // barriers, TMEM address, abort flag, work-item mailbox
@@ -364,22 +371,51 @@ __device__ __forceinline__ void store8(void* out, int64_t off, const float* v, i
 // items in that order from a device counter, so the heads in flight at any time are a
 // few consecutive ones (their K/V stay in L2) and the longest items start first.
 struct ItemGeo {
-    int b, h;
+    int b, h;         // tile A's batch and head
+    int b1, h1;       // tile B's (packed items: the next (batch, head) pair; else b, h)
     int q0a, q0b;     // first query row of tile A / B
     int kb0, kb1;     // first visible key of tile A / B (sliding window)
     int ke0, ke1;     // key end of tile A / B
     int t_begin;      // first key tile (tile A's window start)
     int nt0, nt1;     // key tiles of tile A / B from t_begin (0: tile beyond S)
     int n_max;
-    bool uniform;     // no valid key (key_len <= 0): every key weighs the same
+    bool uniform;     // tile A has no valid key (key_len <= 0): every key weighs the same
+    bool uniform1;    // the same for tile B
 };
 
 __device__ __forceinline__ ItemGeo item_geo(int w, int n_pairs, int tiles, int Hq, int S, int causal, int window,
-                                            const int32_t* key_len) {
+                                            const int32_t* key_len, int packed, int n_heads_total) {
     ItemGeo g;
+    if (packed) {
+        // two (batch, head) pairs of one 128-row tile each, the whole (<= 128-key) sequence visible
+        const int bh0 = 2 * w, bh1 = 2 * w + 1;
+        g.b = bh0 / Hq;
+        g.h = bh0 - g.b * Hq;
+        const bool has1 = bh1 < n_heads_total;
+        g.b1 = has1 ? bh1 / Hq : g.b;
+        g.h1 = has1 ? bh1 - g.b1 * Hq : g.h;
+        g.q0a = g.q0b = 0;
+        g.kb0 = g.kb1 = 0;
+        g.ke0 = g.ke1 = S;
+        g.uniform = g.uniform1 = false;
+        if (key_len != nullptr) {
+            const int kl0 = key_len[g.b], kl1 = key_len[g.b1];
+            if (kl0 <= 0) g.uniform = true;
+            else g.ke0 = min(kl0, S);
+            if (kl1 <= 0) g.uniform1 = true;
+            else g.ke1 = min(kl1, S);
+        }
+        g.t_begin = 0;
+        g.nt0 = 1;
+        g.nt1 = has1 ? 1 : 0;
+        g.n_max = 1;
+        return g;
+    }
     const int x = w % n_pairs, rest = w / n_pairs;
     g.h = rest % Hq;
     g.b = rest / Hq;
+    g.b1 = g.b;
+    g.h1 = g.h;
     const int pair = causal ? n_pairs - 1 - x : x;
     g.q0a = pair * tiles * kBM;
     g.q0b = tiles == 2 ? g.q0a + kBM : S;  // a single-tile item's tile B lies past the sequence
@@ -398,6 +434,7 @@ __device__ __forceinline__ ItemGeo item_geo(int w, int n_pairs, int tiles, int H
         if (kl <= 0) g.uniform = true;
         else g.ke0 = g.ke1 = min(kl, S);
     }
+    g.uniform1 = g.uniform;
     g.t_begin = g.kb0 / kBN;  // tile A starts no later than tile B
     g.nt0 = (g.ke0 + kBN - 1) / kBN - g.t_begin;  // q0a < S for every item
     g.nt1 = g.q0b < S ? (g.ke1 + kBN - 1) / kBN - g.t_begin : 0;
@@ -414,6 +451,8 @@ constexpr int kSlotKb0 = 5, kSlotKb1 = 6, kSlotKe0 = 7, kSlotKe1 = 8;
 constexpr int kSlotTBegin = 9, kSlotNt0 = 10, kSlotNt1 = 11, kSlotUniform = 12;
 // key tiles starting in [kSlotIntLo_t, kSlotIntHi_t] are interior for every row of tile t
 constexpr int kSlotIntLo0 = 13, kSlotIntHi0 = 14, kSlotIntLo1 = 15, kSlotIntHi1 = 16;
+// tile B's batch, head and uniform flag (differ from tile A's for packed items)
+constexpr int kSlotB1 = 17, kSlotH1 = 18, kSlotUniform1 = 19;
 constexpr int kSlotInts = 24;
 
 __device__ __forceinline__ void publish_item(volatile int* ms, bool valid, const ItemGeo& g, int causal, int window) {
@@ -431,6 +470,9 @@ __device__ __forceinline__ void publish_item(volatile int* ms, bool valid, const
     ms[kSlotNt0] = g.nt0;
     ms[kSlotNt1] = g.nt1;
     ms[kSlotUniform] = g.uniform ? 1 : 0;
+    ms[kSlotB1] = g.b1;
+    ms[kSlotH1] = g.h1;
+    ms[kSlotUniform1] = g.uniform1 ? 1 : 0;
     // a key tile [n0, n0 + 128) needs no per-element mask when it lies inside the key range,
     // wholly at or below the diagonal of the tile's first row and wholly inside the window of
     // its last row
@@ -441,7 +483,7 @@ __device__ __forceinline__ void publish_item(volatile int* ms, bool valid, const
             hi = min(hi, q_first - kBN + 1);
             if (window > 0) lo = max(lo, q_last - window + 1);
         }
-        if (g.uniform) {
+        if (t ? g.uniform1 : g.uniform) {
             lo = 1;
             hi = 0;
         }
@@ -463,24 +505,26 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const uint32_t sQ = base + Gm::oQ, sK = base + Gm::oK, sV = base + Gm::oV;
     const uint32_t bar0 = base + Gm::oBar;
     // barriers, 8 bytes each.  Every phase count runs on across the CTA's work items.
-    // Q_t: loaded per item, released by the commit after the item's last QK of tile t
-    auto bQfull = [&](int t) { return bar0 + 8u * (0 + t); };
-    auto bQempty = [&](int t) { return bar0 + 8u * (2 + t); };
+    // Q tile qs = (item % kQBuf) * kTiles + t: loaded per item, released by the commit after the
+    // item's last QK of tile t
+    auto bQfull = [&](int qs) { return bar0 + 8u * (0 + qs); };
+    auto bQempty = [&](int qs) { return bar0 + 8u * (4 + qs); };
     // Ring item i of a work item holds K(i) (i < n_max) and V(i-1) (i >= 1): step j reads
     // V(j) and then K(j+1), both last in the same step, so one stage, one full and one
     // empty barrier serve the pair (one wait and one release per step on the MMA thread).
     // The ring's item count g runs across work items: K and V of ring item g sit in stage
     // g % ST of the K and V rings.
-    auto bKVfull = [&](int s) { return bar0 + 8u * (4 + s); };
-    auto bKVempty = [&](int s) { return bar0 + 8u * (4 + ST + s); };
-    auto bSfull = [&](int t) { return bar0 + 8u * (4 + 2 * ST + t); };
-    auto bPfull = [&](int t) { return bar0 + 8u * (6 + 2 * ST + t); };
-    auto bOdone = [&](int t) { return bar0 + 8u * (8 + 2 * ST + t); };
+    auto bKVfull = [&](int s) { return bar0 + 8u * (8 + s); };
+    auto bKVempty = [&](int s) { return bar0 + 8u * (8 + ST + s); };
+    auto bSfull = [&](int t) { return bar0 + 8u * (8 + 2 * ST + t); };
+    auto bPfull = [&](int t) { return bar0 + 8u * (10 + 2 * ST + t); };
+    auto bOdone = [&](int t) { return bar0 + 8u * (12 + 2 * ST + t); };
     // work-item mailbox: the producer publishes item k in slot k % 2; the MMA warp and the
     // eight softmax warps each release it once read
-    auto bItemFull = [&](int s) { return bar0 + 8u * (10 + 2 * ST + s); };
-    auto bItemEmpty = [&](int s) { return bar0 + 8u * (12 + 2 * ST + s); };
-    const uint32_t bDrain = bar0 + 8u * (14 + 2 * ST);
+    auto bItemFull = [&](int s) { return bar0 + 8u * (14 + 2 * ST + s); };
+    auto bItemEmpty = [&](int s) { return bar0 + 8u * (16 + 2 * ST + s); };
+    const uint32_t bDrain = bar0 + 8u * (18 + 2 * ST);
+    static_assert(8 * (19 + 2 * ST) <= 256, "barriers fit below the TMEM address word");
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(base_ptr + Gm::oBar + 256);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(base_ptr + Gm::oBar + 264);
     // mailbox slot s: kSlotInts ints at oBar + 288 + 4 kSlotInts s, a work item's geometry
@@ -494,9 +538,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     int* const status = p.status;
 
     if (tid == 0) {
+        for (int qs = 0; qs < Gm::kQTiles; ++qs) {
+            mbar_init(bQfull(qs), 1);
+            mbar_init(bQempty(qs), 1);
+        }
         for (int t = 0; t < 2; ++t) {
-            mbar_init(bQfull(t), 1);
-            mbar_init(bQempty(t), 1);
             mbar_init(bSfull(t), 1);
             mbar_init(bPfull(t), 128);
             mbar_init(bOdone(t), 1);
@@ -531,30 +577,40 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             const int32_t* const key_len = p.key_len;
             int* const sched = p.sched;
             const int n_pairs = (S + Gm::kTiles * kBM - 1) / (Gm::kTiles * kBM);
+            const int packed = Gm::kTiles == 2 ? p.packed : 0, n_heads_total = p.B * Hq;
             int k = 0;        // work items published
             int g = 0;        // ring items issued
             int q_items = 0;  // work items whose Q tiles were issued
             const int skip_g = (p.stall && blockIdx.x == 0) ? 1 : -1;  // test hook: a copy never issued
+            // The next item's index is fetched one item ahead, and its geometry (key-length reads)
+            // before the wait for a free mailbox slot: the counter's atomic and those reads take
+            // microseconds, which would otherwise separate short items.  Packed items (uniform
+            // cost) are assigned statically: CTA c takes items c, c + grid, ...
+            int w_next = packed ? (int)blockIdx.x : atomicAdd(sched, 1);
             for (;; ++k) {
+                const int w = w_next;
+                const ItemGeo it = item_geo(w < n_items ? w : 0, n_pairs, Gm::kTiles, Hq, S, causal, window, key_len,
+                                            packed, n_heads_total);
+                if (w < n_items) w_next = packed ? w + (int)gridDim.x : atomicAdd(sched, 1);
                 const int slot = k & 1;
                 // slot k % 2 is free once every reader of item k-2 is done with it
                 if (k >= 2 && !mbar_wait(bItemEmpty(slot), ((k >> 1) - 1) & 1, abort_flag, status)) break;
-                const int w = atomicAdd(sched, 1);
-                const ItemGeo it = item_geo(w < n_items ? w : 0, n_pairs, Gm::kTiles, Hq, S, causal, window, key_len);
                 publish_item(slots + kSlotInts * slot, w < n_items, it, causal, window);
                 mbar_arrive(bItemFull(slot));  // release: the slot's values are visible to the waiters
                 if (w >= n_items) break;
-                const int kvh = it.h / G;
+                const int kvh = it.h / G, kvh1 = it.h1 / G;
                 bool ok = true;
+                const int qb = k % Gm::kQBuf;
                 for (int t = 0; t < Gm::kTiles && ok; ++t) {
-                    if (k >= 1 && !mbar_wait(bQempty(t), (k - 1) & 1, abort_flag, status)) {
+                    const int qs = qb * Gm::kTiles + t;
+                    if (k >= Gm::kQBuf && !mbar_wait(bQempty(qs), ((k / Gm::kQBuf) - 1) & 1, abort_flag, status)) {
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(bQfull(t), Gm::kTileBytes);
+                    mbar_expect_tx(bQfull(qs), Gm::kTileBytes);
                     for (int pn = 0; pn < NP; ++pn)
-                        tma_load_4d(sQ + t * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmQ, bQfull(t), 64 * pn, it.h,
-                                    t ? it.q0b : it.q0a, it.b);
+                        tma_load_4d(sQ + qs * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmQ, bQfull(qs), 64 * pn,
+                                    t ? it.h1 : it.h, t ? it.q0b : it.q0a, t ? it.b1 : it.b);
                 }
                 if (!ok) break;
                 q_items = k + 1;
@@ -567,6 +623,21 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                         break;
                     }
                     if (g == skip_g) {  // nothing is issued for it: its consumer's wait runs out
+                        ++g;
+                        continue;
+                    }
+                    if (packed) {
+                        // ring item 0: K of tile A's head in the K slot, K of tile B's in the V slot;
+                        // ring item 1: V of tile A's head in the V slot, V of tile B's in the K slot
+                        const bool two = it.nt1 > 0;
+                        mbar_expect_tx(bKVfull(st), two ? 2u * Gm::kTxTile : Gm::kTxTile);
+                        const CUtensorMap* const m = i == 0 ? &tmK : &tmV;
+                        const uint32_t dst_a = (i == 0 ? sK : sV) + st * Gm::kTileBytes;
+                        const uint32_t dst_b = (i == 0 ? sV : sK) + st * Gm::kTileBytes;
+                        for (int pn = 0; pn < NP; ++pn) {
+                            tma_load_4d(dst_a + pn * Gm::kPanelBytes, m, bKVfull(st), 64 * pn, kvh, 0, it.b);
+                            if (two) tma_load_4d(dst_b + pn * Gm::kPanelBytes, m, bKVfull(st), 64 * pn, kvh1, 0, it.b1);
+                        }
                         ++g;
                         continue;
                     }
@@ -585,8 +656,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 if (!ok) break;
             }
             // every copy this thread issued lands before the CTA may exit
-            if (q_items > 0)
-                for (int t = 0; t < Gm::kTiles; ++t) mbar_drain(bQfull(t), (q_items - 1) & 1);
+            for (int j = q_items > Gm::kQBuf ? q_items - Gm::kQBuf : 0; j < q_items; ++j)
+                for (int t = 0; t < Gm::kTiles; ++t)
+                    mbar_drain(bQfull((j % Gm::kQBuf) * Gm::kTiles + t), (j / Gm::kQBuf) & 1);
             for (int i = (g > ST ? g - ST : 0); i < g; ++i)
                 if (i != skip_g) mbar_drain(bKVfull(i % ST), (i / ST) & 1);
         }
@@ -615,12 +687,18 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             // 14-bit start-address field (addr >> 4) of the low word, and every offset here stays inside it
             const uint64_t dQ = smem_desc(sQ, 16, 1024), dK = smem_desc(sK, 16, 1024);
             const uint64_t dV = smem_desc(sV, Gm::kPanelBytes, 1024);
-            const uint32_t q_lo = (uint32_t)dQ, k_lo = (uint32_t)dK, v_lo = (uint32_t)dV;
+            const uint32_t q_lo = (uint32_t)dQ, v_lo = (uint32_t)dV;
             const uint32_t qk_hi = (uint32_t)(dQ >> 32), v_hi = (uint32_t)(dV >> 32);  // dK's high word is dQ's
+            // packed items: tile B's K sits in the V slot (read K-major) and its V in the K slot (read MN-major)
+            const bool packed = Gm::kTiles == 2 && p.packed != 0;
+            const uint32_t k_lo_b = packed ? (uint32_t)smem_desc(sV, 16, 1024) : (uint32_t)dK;
+            const uint32_t v_lo_b = packed ? (uint32_t)smem_desc(sK, Gm::kPanelBytes, 1024) : v_lo;
+            const uint32_t k_lo = (uint32_t)dK;
             // S_t = Q_t K^T with K in ring stage st
+            int qb = 0;  // Q buffer of the current item
             auto issue_qk = [&](int t, int st) {
-                const uint32_t a0 = q_lo + (uint32_t)(t * Gm::kTileBytes >> 4);
-                const uint32_t b0 = k_lo + (uint32_t)(st * Gm::kTileBytes >> 4);
+                const uint32_t a0 = q_lo + (uint32_t)((qb * Gm::kTiles + t) * Gm::kTileBytes >> 4);
+                const uint32_t b0 = (t ? k_lo_b : k_lo) + (uint32_t)(st * Gm::kTileBytes >> 4);
                 const uint32_t d = tmem + 128u * t;
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ++ks) {
@@ -633,7 +711,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             // O_t (+)= P_t V with V in ring stage st, MN-major: 8-key atoms 1024 B apart (SBO),
             // 64-column panels kPanelBytes apart (LBO)
             auto issue_pv = [&](int t, int st, uint32_t acc) {
-                const uint32_t b0 = v_lo + (uint32_t)(st * Gm::kTileBytes >> 4);
+                const uint32_t b0 = (t ? v_lo_b : v_lo) + (uint32_t)(st * Gm::kTileBytes >> 4);
                 const uint32_t d = tmem + Gm::kOcol + 128u * t, a = tmem + 128u * t;
                 umma_ts_w<-1>(ln, d, a, b0, v_hi, idp, acc);
 #pragma unroll
@@ -648,15 +726,17 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 volatile int* const ms = slots + kSlotInts * slot;
                 if (!ms[kSlotValid]) break;
                 const int nt0 = ms[kSlotNt0], nt1 = ms[kSlotNt1], n_max = max(nt0, nt1);
-                ok = __all_sync(0xffffffffu, mbar_wait(bQfull(0), k & 1, abort_flag, status) &&
-                                                 (Gm::kTiles == 1 || mbar_wait(bQfull(1), k & 1, abort_flag, status)));
+                qb = k % Gm::kQBuf;
+                const int qpar = (k / Gm::kQBuf) & 1, qs0 = qb * Gm::kTiles;
+                ok = __all_sync(0xffffffffu, mbar_wait(bQfull(qs0), qpar, abort_flag, status) &&
+                                                 (Gm::kTiles == 1 || mbar_wait(bQfull(qs0 + 1), qpar, abort_flag, status)));
                 if (ok) ok = wait_item(g);
                 if (!ok) break;
                 // S_t(0); a tile with at most one key tile reads Q_t for the last time here
                 if (nt0 > 0) issue_qk(0, g % ST);
-                if (nt0 <= 1) umma_commit_w(ln, bQempty(0));
+                if (nt0 <= 1) umma_commit_w(ln, bQempty(qs0));
                 if (nt1 > 0) issue_qk(1, g % ST);
-                if (Gm::kTiles == 2 && nt1 <= 1) umma_commit_w(ln, bQempty(1));
+                if (Gm::kTiles == 2 && nt1 <= 1) umma_commit_w(ln, bQempty(qs0 + 1));
                 umma_commit_w(ln, bKVempty(g % ST));  // ring item 0 (K(0)) read by both tiles
                 for (int j = 0; j < n_max && ok; ++j) {
                     const int st = (g + j + 1) % ST;  // ring item j+1: V(j), K(j+1)
@@ -685,7 +765,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                         if (j + 1 == ntt) umma_commit_w(ln, bOdone(t));
                         if (j + 1 < ntt) {
                             issue_qk(t, st);
-                            if (j + 2 == ntt) umma_commit_w(ln, bQempty(t));  // the item's last QK of tile t
+                            if (j + 2 == ntt) umma_commit_w(ln, bQempty(qs0 + t));  // the item's last QK of tile t
                         }
                         if (t == rel) umma_commit_w(ln, bKVempty(st));
                     }
@@ -733,8 +813,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             }
             // key tiles starting in [int_lo, int_hi] need no per-element mask
             const int int_lo = ms[t ? kSlotIntLo1 : kSlotIntLo0], int_hi = ms[t ? kSlotIntHi1 : kSlotIntHi0];
-            const bool uniform = ms[kSlotUniform] != 0;
-            const float* const mrow0 = kAdditive ? mask + (int64_t)ms[kSlotB] * S : nullptr;
+            const bool uniform = ms[t ? kSlotUniform1 : kSlotUniform] != 0;
+            const float* const mrow0 = kAdditive ? mask + (int64_t)ms[t ? kSlotB1 : kSlotB] * S : nullptr;
             const float edge_mult = uniform ? 0.f : sl2;
             const bool additive = kAdditive && !uniform;
             float m_run = -INFINITY, l_run = 0.f;
@@ -852,7 +932,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                     tmem_ld32(o_addr + 32 * c, r);
                     tmem_wait_ld();
                     if (q < S) {
-                        const int64_t off = ms[kSlotB] * p.o_sb + (int64_t)q * p.o_ss + ms[kSlotH] * p.o_sh + 32 * c;
+                        const int64_t off = ms[t ? kSlotB1 : kSlotB] * p.o_sb + (int64_t)q * p.o_ss +
+                                            ms[t ? kSlotH1 : kSlotH] * p.o_sh + 32 * c;
 #pragma unroll
                         for (int i = 0; i < 32; i += 8) {
                             float v[8];
@@ -953,8 +1034,13 @@ cudaError_t kernel_ready_for(const AttnParams& p) {
     return p.mask != nullptr ? kernel_ready<D, true>() : kernel_ready<D, false>();
 }
 
-// query-tile pairs x heads x batch
+// Bidirectional sequences of at most one tile with two query tiles per item (head dim <= 128)
+// pack two (batch, head) pairs into each item.
+bool packed_items(const AttnParams& a) { return !a.causal && a.S <= kBM && a.D <= 128; }
+
+// query-tile pairs x heads x batch, or (packed) pairs of (batch, head)
 int64_t work_items(const AttnParams& a) {
+    if (packed_items(a)) return ((int64_t)a.Hq * a.B + 1) / 2;
     const int rows = (a.D <= 128 ? 2 : 1) * kBM;  // TcGeo<D>::kTiles query tiles per item
     return (int64_t)((a.S + rows - 1) / rows) * a.Hq * a.B;
 }
@@ -994,6 +1080,7 @@ cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream, b
     p.sched = status + kStatusSchedWord;
     p.n_items = (int)work_items(a);
     p.stall = stall ? 1 : 0;
+    p.packed = packed_items(a) ? 1 : 0;
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
                                                   cudaSuccess || sms <= 0)
