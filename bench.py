@@ -248,7 +248,9 @@ class DecodeWorkload:
         self.h_lens = pin(self.lens_d)
         self.h_out = [torch.empty(B, Hq, D).pin_memory() for _ in self.layers]
         if world > 1:  # every rank receives the whole batch's outputs of both layers
+            from b200attn import sharding
             self.h_out_all = torch.empty(len(self.layers), B * world, Hq, D).pin_memory()
+            self.reassemble = sharding.Reassembly(self.plan, torch.device("cuda", torch.cuda.current_device()))
 
     def tokens_per_step(self):
         return self.seqs_per_rank
@@ -298,9 +300,8 @@ class DecodeWorkload:
         if self.world > 1:
             # output reassembly: one NCCL all-gather of the equal shards (both layers at once),
             # scattered back into unit order, then the whole batch's outputs to the host
-            from b200attn import sharding
             local = self.torch.stack(self.out, dim=1)  # [units, layers, G, D]
-            full = sharding.gather_shards(local, self.plan)
+            full = self.reassemble(local)
             self.h_out_all.copy_(full.transpose(0, 1), non_blocking=True)
 
     def e2e_bytes(self):

@@ -303,6 +303,33 @@ B2A_API int b2a_gemma_fused_attention_context(b2a_context* ctx, const float* q, 
                                               int groups_per_kv, int head_dim, int kv_dim,
                                               int first_valid, int query_pos, float scale, void* stream);
 
+/* ------------------------------------------------ projections around attention */
+
+/* y[M,N] = x[M,K] w[N,K]^T + bias[N] + residual[M,N] on the tensor cores (tcgen05, TMEM
+ * accumulator, TMA-staged tiles), bias and residual fused into the epilogue: the O
+ * projection with the residual add (residual1 = input + oProjOut; decode
+ * INF/qwen/Qwen2Runtime.java:756-777, prefill L973-1000) and the QKV projection with its
+ * bias (decode L693-716, prefill L888-914).  x and w: FLOAT16 or BFLOAT16 (one type), row-major, K a
+ * multiple of 8; bias: float [N] or NULL; residual: [M,N] of out_dtype or NULL (may
+ * alias y); fp32 accumulation. */
+B2A_API int b2a_linear(b2a_context* ctx, int in_dtype, int out_dtype, const void* x, const void* w,
+                       const float* bias, const void* residual, void* y, int M, int N, int K, void* stream);
+
+/* One decode-layer attention block, Qwen2Runtime.processLayerDecode from the normed input
+ * to the first residual (INF/qwen/Qwen2Runtime.java:693-777), in three launches: the QKV
+ * projection with its bias (fp32 rows [Q | K | V]), the fused decode step (NeoX RoPE at
+ * ctx_lens[b], KV append, GQA attention; as b2a_decode) reading those rows directly, and
+ * the O projection with the residual add.
+ *   x [B, hidden], w_qkv [(Hq + 2 Hkv) D, hidden], w_o [hidden, Hq D], residual / y
+ *   [B, hidden]: act_dtype (FLOAT16 / BFLOAT16); b_qkv float [(Hq + 2 Hkv) D] or NULL;
+ *   caches as b2a_decode.  The attention output feeding the O projection is rounded to
+ *   act_dtype (the operand type of its tensor-core GEMM). */
+B2A_API int b2a_decode_attention_block(b2a_context* ctx, int act_dtype, int cache_dtype, const void* x,
+                                       const void* w_qkv, const float* b_qkv, void* k_cache, void* v_cache,
+                                       int kv_layout, const int32_t* ctx_lens, const void* w_o, const void* residual,
+                                       void* y, int B, int hidden, int Hq, int Hkv, int D, int max_seq, float scale,
+                                       double rope_theta, int window, void* stream);
+
 /* ------------------------------------------------------------ multi-GPU */
 
 /* One process driving several GPUs of a node: the multi-device counterpart of

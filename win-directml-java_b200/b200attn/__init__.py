@@ -108,6 +108,9 @@ def lib() -> ctypes.CDLL:
                                         _vp, _f, _vp, _vp]
         L.b2a_gemma_fused_attention_context.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp]
         L.b2a_partition_units.argtypes = [_i, _i, _vp, _vp]
+        L.b2a_linear.argtypes = [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]
+        L.b2a_decode_attention_block.argtypes = [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _i,
+                                                 _i, _i, _i, _i, _f, _d, _i, _vp]
         L.b2a_group_create.argtypes = [_i, _vp, ctypes.POINTER(_vp)]
         L.b2a_group_destroy.argtypes = [_vp]
         L.b2a_group_last_error.argtypes = [_vp, ctypes.c_char_p, ctypes.c_size_t]
@@ -121,7 +124,7 @@ def lib() -> ctypes.CDLL:
                      "b2a_reserve_decode", "b2a_check_device_status", "b2a_mha", "b2a_prefill_causal", "b2a_decode",
                      "b2a_qwen_rope_and_append", "b2a_qwen_gqa_attention_decode", "b2a_qwen_decode_step", "b2a_prefill_gemma",
                      "b2a_gemma_fused_attention_context", "b2a_partition_units", "b2a_test_inject_wait_timeout",
-                     "b2a_group_create", "b2a_group_destroy", "b2a_group_last_error", "b2a_group_size",
+                     "b2a_linear", "b2a_decode_attention_block", "b2a_group_create", "b2a_group_destroy", "b2a_group_last_error", "b2a_group_size",
                      "b2a_group_context", "b2a_group_check_device_status", "b2a_sharded_decode", "b2a_sharded_mha"):
             getattr(L, name).restype = _i
         _lib = L
@@ -313,6 +316,35 @@ def decode(ctx: Context, q_new, k_new, v_new, k_cache, v_cache, ctx_lens, o, sca
                                Hkv, D, max_seq, scale, rope_mode, rope_theta, window, _ptr(q_norm_w), _ptr(k_norm_w),
                                norm_eps, _ptr(o), _stream(stream)))
     return o
+
+
+def linear(ctx: Context, x, w, y, bias=None, residual=None, stream=None):
+    """y = x w^T + bias + residual on the tensor cores (x [M,K], w [N,K] fp16/bf16; bias float [N];
+    residual and y [M,N]); the O projection with its residual add, the QKV projection with its bias."""
+    M, K = x.shape
+    N = w.shape[0]
+    if tuple(w.shape) != (N, K) or tuple(y.shape) != (M, N):
+        raise ValueError("w must be [N,K] and y [M,N] for x [M,K]")
+    if residual is not None and tuple(residual.shape) != (M, N):
+        raise ValueError("residual must be [M,N]")
+    ctx.check(lib().b2a_linear(ctx.handle, _dtype_code(x), _dtype_code(y), _ptr(x), _ptr(w), _ptr(bias),
+                               _ptr(residual), _ptr(y), M, N, K, _stream(stream)))
+    return y
+
+
+def decode_attention_block(ctx: Context, x, w_qkv, b_qkv, k_cache, v_cache, ctx_lens, w_o, residual, y, *,
+                           num_q_heads: int, num_kv_heads: int, scale: float, rope_theta: float,
+                           kv_layout: int = KV_HEAD_MAJOR, window: int = 0, stream=None):
+    """One decode-layer attention block (Qwen2Runtime.processLayerDecode, normed input to residual 1):
+    QKV projection + bias, NeoX RoPE at ctx_lens, KV append, GQA attention, O projection + residual."""
+    B, hidden = x.shape
+    D = w_qkv.shape[0] // (num_q_heads + 2 * num_kv_heads)
+    max_seq = k_cache.shape[2] if kv_layout == KV_HEAD_MAJOR else k_cache.shape[1]
+    ctx.check(lib().b2a_decode_attention_block(
+        ctx.handle, _dtype_code(x), _dtype_code(k_cache), _ptr(x), _ptr(w_qkv), _ptr(b_qkv), _ptr(k_cache),
+        _ptr(v_cache), kv_layout, _ptr(ctx_lens), _ptr(w_o), _ptr(residual), _ptr(y), B, hidden, num_q_heads,
+        num_kv_heads, D, max_seq, scale, rope_theta, window, _stream(stream)))
+    return y
 
 
 def _ptr_array(tensors):

@@ -30,27 +30,41 @@ def _device_of(group):
         else torch.device("cpu")
 
 
+class Reassembly:
+    """Output reassembly for one plan, set up once: one all-gather of the equal shards into a
+    single buffer (rank-major), then one index copy back into unit order on the receiving
+    device.  The unit-order index lives on the device, so a call issues no host-device copy
+    and no synchronisation."""
+
+    def __init__(self, plan: list[np.ndarray], device):
+        import torch
+        counts = {len(p) for p in plan}
+        if len(counts) != 1:
+            raise ValueError("gather_shards needs equal shard sizes (use plan_shards)")
+        self.world, self.per = len(plan), counts.pop()
+        # gathered row i holds unit order[i]
+        self.order = torch.as_tensor(np.concatenate(plan), dtype=torch.long, device=device)
+
+    def __call__(self, local, group=None):
+        import torch
+        import torch.distributed as dist
+        if local.shape[0] != self.per:
+            raise ValueError("local results do not match this rank's shard size")
+        buf = local.new_empty((self.world * self.per,) + tuple(local.shape[1:]))
+        dist.all_gather_into_tensor(buf, local.contiguous(), group=group)
+        out = torch.empty_like(buf)
+        out.index_copy_(0, self.order, buf)
+        return out
+
+
 def gather_shards(local, plan: list[np.ndarray], group=None):
     """Reassembles per-rank results into global unit order on every rank.
 
     local: this rank's results, [len(plan[rank]), ...] in the order of plan[rank].
-    Returns [n_units, ...].  Shards are equal in size (plan_shards), so one all_gather
-    moves them; the scatter back into unit order happens on the receiving device."""
-    import torch
-    import torch.distributed as dist
-    world = len(plan)
-    counts = {len(p) for p in plan}
-    if len(counts) != 1:
-        raise ValueError("gather_shards needs equal shard sizes (use plan_shards)")
-    if local.shape[0] != counts.pop():
-        raise ValueError("local results do not match this rank's shard size")
-    parts = [torch.empty_like(local) for _ in range(world)]
-    dist.all_gather(parts, local.contiguous(), group=group)
-    n = sum(len(p) for p in plan)
-    out = local.new_empty((n,) + tuple(local.shape[1:]))
-    for r in range(world):
-        out[torch.as_tensor(plan[r], device=local.device, dtype=torch.long)] = parts[r]
-    return out
+    Returns [n_units, ...].  Shards are equal in size (plan_shards), so one all-gather
+    moves them; the scatter back into unit order happens on the receiving device.  A
+    caller that reassembles every step builds a Reassembly once instead."""
+    return Reassembly(plan, local.device)(local, group)
 
 
 def max_over_ranks(values, group=None) -> list[float]:

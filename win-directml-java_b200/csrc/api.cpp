@@ -36,6 +36,9 @@ struct b2a_context {
     // prefill workspace: rope table + rotated q/k staging
     void* pf_ws = nullptr;
     size_t pf_ws_bytes = 0;
+    // attention block: the QKV projection's fp32 rows and the attention output
+    void* blk_ws = nullptr;
+    size_t blk_ws_bytes = 0;
     // generic-kernel key split: [counters][partial slots], the same layout rules as dec_ws
     void* split_ws = nullptr;
     size_t split_ws_bytes = 0;
@@ -87,7 +90,7 @@ size_t dtype_size(int d) { return d == B2A_FLOAT32 ? 4 : 2; }
 
 int ensure_buffer(b2a_context* ctx, void** buf, size_t* have, size_t need, const char* what) {
     if (*have >= need) return B2A_OK;
-    const size_t other = ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes - *have;
+    const size_t other = ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes + ctx->blk_ws_bytes - *have;
     if (ctx->ws_limit != 0 && need + other > ctx->ws_limit)
         return fail(ctx, B2A_EOOM, "%s workspace of %zu bytes exceeds the context limit of %zu bytes", what,
                     need + other, ctx->ws_limit);
@@ -299,6 +302,7 @@ B2A_API int b2a_destroy(b2a_context* ctx) {
         if (ctx->dec_ws) cudaFree(ctx->dec_ws);
         if (ctx->pf_ws) cudaFree(ctx->pf_ws);
         if (ctx->split_ws) cudaFree(ctx->split_ws);
+        if (ctx->blk_ws) cudaFree(ctx->blk_ws);
     }
     delete ctx;
     return B2A_OK;
@@ -322,7 +326,7 @@ B2A_API int b2a_set_workspace_limit(b2a_context* ctx, size_t bytes) {
 
 B2A_API int b2a_workspace_bytes(const b2a_context* ctx, size_t* bytes) {
     if (!ctx || !bytes) return B2A_EINVAL;
-    *bytes = ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes;
+    *bytes = ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes + ctx->blk_ws_bytes;
     return B2A_OK;
 }
 
@@ -865,6 +869,114 @@ B2A_API int b2a_gemma_fused_attention_context(b2a_context* ctx, const float* q, 
     p.out = ctx_out;
     p.out_dtype = B2A_FLOAT32;
     return run_decode(ctx, p, static_cast<cudaStream_t>(stream), false);
+}
+
+// ----------------------------------------------------------------- projections
+B2A_API int b2a_linear(b2a_context* ctx, int in_dtype, int out_dtype, const void* x, const void* w, const float* bias,
+                       const void* residual, void* y, int M, int N, int K, void* stream) {
+    if (!ctx) return B2A_EINVAL;
+    if (!x || !w || !y) return fail(ctx, B2A_EINVAL, "x, w and y must not be null");
+    if (in_dtype != B2A_FLOAT16 && in_dtype != B2A_BFLOAT16)
+        return fail(ctx, B2A_ENOTSUP, "b2a_linear multiplies 16-bit operands (FLOAT16 or BFLOAT16), got %d", in_dtype);
+    if (!valid_dtype(out_dtype)) return fail(ctx, B2A_EINVAL, "unsupported output element type %d", out_dtype);
+    if (M <= 0 || N <= 0 || K <= 0) return fail(ctx, B2A_EINVAL, "M, N and K must be > 0");
+    if (K % 8 != 0) return fail(ctx, B2A_EINVAL, "K must be a multiple of 8 (16-byte rows for the TMA loads)");
+    DeviceGuard guard(ctx->device);
+    if (!linear_tc_supported(in_dtype, K, K, K, x, w))
+        return fail(ctx, B2A_EINVAL, "x and w must be 16-byte aligned");
+    LinearArgs a{};
+    a.x = x;
+    a.ldx = K;
+    a.w = w;
+    a.ldw = K;
+    a.in_dtype = in_dtype;
+    a.bias = bias;
+    a.residual = residual;
+    a.ldr = N;
+    a.y = y;
+    a.ldy = N;
+    a.out_dtype = out_dtype;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    const cudaError_t e = launch_linear_tc(a, ctx->status, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "linear kernel launch");
+    return B2A_OK;
+}
+
+B2A_API int b2a_decode_attention_block(b2a_context* ctx, int act_dtype, int cache_dtype, const void* x,
+                                       const void* w_qkv, const float* b_qkv, void* k_cache, void* v_cache,
+                                       int kv_layout, const int32_t* ctx_lens, const void* w_o, const void* residual,
+                                       void* y, int B, int hidden, int Hq, int Hkv, int D, int max_seq, float scale,
+                                       double rope_theta, int window, void* stream) {
+    // Qwen2Runtime.processLayerDecode from the normed input to residual 1
+    // (INF/qwen/Qwen2Runtime.java:693-777): QKV projection + bias, RoPE, KV append, GQA
+    // attention, O projection + residual, in three launches -- the bias in the QKV GEMM's
+    // epilogue, RoPE and the append in the attention's prologue, the residual in the O GEMM's
+    // epilogue.
+    if (!ctx) return B2A_EINVAL;
+    if (!x || !w_qkv || !k_cache || !v_cache || !ctx_lens || !w_o || !y)
+        return fail(ctx, B2A_EINVAL, "x, w_qkv, caches, ctx_lens, w_o and y must not be null");
+    if (act_dtype != B2A_FLOAT16 && act_dtype != B2A_BFLOAT16)
+        return fail(ctx, B2A_ENOTSUP, "activations and weights must be FLOAT16 or BFLOAT16");
+    int rc = check_heads(ctx, Hq, Hkv);
+    if (rc) return rc;
+    if ((rc = check_head_dim(ctx, D))) return rc;
+    if (B <= 0 || hidden <= 0 || max_seq <= 0) return fail(ctx, B2A_EINVAL, "B, hidden and max_seq must be > 0");
+    if (hidden % 8 != 0 || (Hq * D) % 8 != 0)
+        return fail(ctx, B2A_EINVAL, "hidden and Hq*D must be multiples of 8 (16-byte rows for the TMA loads)");
+    if (!(rope_theta > 0.0)) return fail(ctx, B2A_EINVAL, "rope theta must be > 0");
+    DeviceGuard guard(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int nqkv = (Hq + 2 * Hkv) * D;
+    const size_t qkv_bytes = ((size_t)B * nqkv * 4 + 255) / 256 * 256;
+    const size_t attn_bytes = (size_t)B * Hq * D * 2;
+    rc = ensure_buffer(ctx, &ctx->blk_ws, &ctx->blk_ws_bytes, qkv_bytes + attn_bytes, "attention block");
+    if (rc) return rc;
+    float* qkv = static_cast<float*>(ctx->blk_ws);
+    void* attn = static_cast<char*>(ctx->blk_ws) + qkv_bytes;
+    // 1. qkv = x W_qkv^T + b (fp32 rows [Q | K | V], as the reference keeps them)
+    if ((rc = b2a_linear(ctx, act_dtype, B2A_FLOAT32, x, w_qkv, b_qkv, nullptr, qkv, B, nqkv, hidden, stream)))
+        return rc;
+    // 2. RoPE of q and k at ctx_lens[b], k/v append, attention (the decode kernel reads the fused rows)
+    DecodeParams p{};
+    p.q = qkv;
+    p.k_new = qkv + (int64_t)Hq * D;
+    p.v_new = qkv + (int64_t)(Hq + Hkv) * D;
+    p.q_dtype = B2A_FLOAT32;
+    p.q_seq_stride = p.kv_new_seq_stride = nqkv;
+    p.k_cache = k_cache;
+    p.v_cache = v_cache;
+    p.cache_dtype = cache_dtype;
+    p.stride_b = (int64_t)Hkv * max_seq * D;
+    if (kv_layout == B2A_KV_HEAD_MAJOR) {
+        p.stride_h = (int64_t)max_seq * D;
+        p.stride_pos = D;
+    } else if (kv_layout == B2A_KV_POS_MAJOR) {
+        p.stride_h = D;
+        p.stride_pos = (int64_t)Hkv * D;
+    } else {
+        return fail(ctx, B2A_EINVAL, "unknown kv layout %d", kv_layout);
+    }
+    if (!valid_dtype(cache_dtype)) return fail(ctx, B2A_EINVAL, "unsupported cache element type %d", cache_dtype);
+    p.ctx_lens = ctx_lens;
+    p.B = B;
+    p.Hq = Hq;
+    p.Hkv = Hkv;
+    p.G = Hq / Hkv;
+    p.D = D;
+    p.max_seq = max_seq;
+    p.window = window;
+    p.first_explicit = -1;
+    p.append = 1;
+    p.rope_mode = B2A_ROPE_NEOX;
+    inv_freq_table(rope_theta, D, p.inv_freq);
+    p.scale = scale;
+    p.out = attn;
+    p.out_dtype = act_dtype;
+    if ((rc = run_decode(ctx, p, s, true))) return rc;
+    // 3. y = attn W_o^T + residual
+    return b2a_linear(ctx, act_dtype, act_dtype, attn, w_o, nullptr, residual, y, B, hidden, Hq * D, stream);
 }
 
 // ----------------------------------------------------------------- sharding

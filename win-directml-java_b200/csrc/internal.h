@@ -160,6 +160,26 @@ cudaError_t launch_norm_rope_rows(const void* src, void* dst, void* dst_in, int 
                                   const double* inv_freq, double2* table, bool build_table, int* status,
                                   cudaStream_t stream);
 
+// y[M][N] = x[M][K] w[N][K]^T (+ bias[N]) (+ residual[M][N]) on the tensor cores: 16-bit x and
+// w of one type (row strides ldx, ldw, multiples of 8 elements), fp32 accumulation, y and the
+// residual in out_dtype (row strides ldy, ldr).
+struct LinearArgs {
+    const void* x;
+    int64_t ldx;
+    const void* w;
+    int64_t ldw;
+    int in_dtype;
+    const float* bias;
+    const void* residual;
+    int64_t ldr;
+    void* y;
+    int64_t ldy;
+    int out_dtype;
+    int M, N, K;
+};
+bool linear_tc_supported(int in_dtype, int K, int64_t ldx, int64_t ldw, const void* x, const void* w);
+cudaError_t launch_linear_tc(const LinearArgs& a, int* status, cudaStream_t stream);
+
 // Sets the message b2a_last_error(NULL, ...) returns on this thread.
 void set_thread_error(const char* msg);
 
