@@ -341,3 +341,27 @@ def test_generic_kernel_runs_unsplit_without_room_for_the_split_workspace():
         assert small.workspace_bytes() <= 4096
         err, _ = assert_close(to_np(y), want, what="unsplit fp32 encoder under a workspace limit")
         assert err < 1e-4
+
+
+def test_fp32_prefill_rotates_in_kernel_from_the_cached_table(ctx):
+    """fp32 NeoX prefill runs as one launch that rotates q and k inside the attention kernel, from a
+    float (cos, sin) table the context keeps across calls: a change of theta, of head dim and a position
+    range beyond the cached one each rebuild it, and every result matches the oracle exactly enough for
+    fp32 end to end."""
+    import torch
+    import b200attn
+    for i, (S, Hq, Hkv, D, theta, pos0) in enumerate([(256, 9, 3, 64, 1e5, 0), (100, 4, 2, 64, 1e4, 300),
+                                                      (300, 4, 1, 64, 1e5, 50), (90, 2, 2, 32, 1e5, 7),
+                                                      (256, 9, 3, 64, 1e5, 0)]):
+        q = normal(600 + i, (1, S, Hq, D), oracle.F32)
+        k = normal(610 + i, (1, S, Hkv, D), oracle.F32)
+        v = normal(620 + i, (1, S, Hkv, D), oracle.F32)
+        scale = float(np.float32(1.0 / math.sqrt(D)))
+        want = oracle.prefill(q, k, v, B=1, S=S, Hq=Hq, Hkv=Hkv, D=D, scale=scale, rope_theta=theta, pos0=pos0)
+        o = torch.full((1, S, Hq, D), float("nan"), dtype=torch.float32, device="cuda")
+        b200attn.prefill_causal(ctx, to_dev(q, oracle.F32), to_dev(k, oracle.F32), to_dev(v, oracle.F32), o, scale,
+                                rope_mode=b200attn.ROPE_NEOX, rope_theta=theta, pos0=pos0)
+        torch.cuda.synchronize()
+        assert ctx.last_attention_kernel() == "generic"
+        err, _ = assert_close(to_np(o), want, what=f"fused-rope fp32 prefill {i}")
+        assert err < 1e-4

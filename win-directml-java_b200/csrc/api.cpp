@@ -36,6 +36,13 @@ struct b2a_context {
     // prefill workspace: rope table + rotated q/k staging
     void* pf_ws = nullptr;
     size_t pf_ws_bytes = 0;
+    // float NeoX (cos, sin) table [position][D/2] for positions [0, rope_npos), reused by later
+    // calls with the same theta and head dim (rebuilt, on the calling stream, when it does not cover)
+    void* rope_tab = nullptr;
+    size_t rope_tab_bytes = 0;
+    double rope_theta = 0.0;
+    int rope_D = 0;
+    int rope_npos = 0;
     // attention block: the QKV projection's fp32 rows and the attention output
     void* blk_ws = nullptr;
     size_t blk_ws_bytes = 0;
@@ -90,7 +97,8 @@ size_t dtype_size(int d) { return d == B2A_FLOAT32 ? 4 : 2; }
 
 int ensure_buffer(b2a_context* ctx, void** buf, size_t* have, size_t need, const char* what) {
     if (*have >= need) return B2A_OK;
-    const size_t other = ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes + ctx->blk_ws_bytes - *have;
+    const size_t other =
+        ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes + ctx->blk_ws_bytes + ctx->rope_tab_bytes - *have;
     if (ctx->ws_limit != 0 && need + other > ctx->ws_limit)
         return fail(ctx, B2A_EOOM, "%s workspace of %zu bytes exceeds the context limit of %zu bytes", what,
                     need + other, ctx->ws_limit);
@@ -133,6 +141,28 @@ void inv_freq_table(double theta, int D, double* out) {
     // 1 / theta^(2i/D) in double (INF/decoderonly/DecoderOnlyRotaryEmbedding.java:57-59,
     // INF/gemma/Gemma3ReferenceMath.java:74)
     for (int i = 0; i < D / 2; ++i) out[i] = 1.0 / pow(theta, (2.0 * i) / D);
+}
+
+// The context's NeoX table covering positions [0, npos) for (theta, D); built on `stream` when the
+// cached one does not cover them.  Calls on other streams must be ordered after this one (the
+// same rule as every workspace of a context).
+int neox_table(b2a_context* ctx, double theta, int D, int npos, cudaStream_t stream, const float2** out) {
+    if (!(ctx->rope_tab != nullptr && ctx->rope_theta == theta && ctx->rope_D == D && ctx->rope_npos >= npos)) {
+        const int n = (npos + 255) / 256 * 256;
+        const int rc = ensure_buffer(ctx, &ctx->rope_tab, &ctx->rope_tab_bytes, (size_t)n * (D / 2) * sizeof(float2),
+                                     "rope table");
+        if (rc) return rc;
+        double inv[kMaxHeadDim / 2];
+        inv_freq_table(theta, D, inv);
+        const cudaError_t e =
+            launch_rope_table_f32(static_cast<float2*>(ctx->rope_tab), n, D / 2, 0, inv, stream);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "rope table launch");
+        ctx->rope_theta = theta;
+        ctx->rope_D = D;
+        ctx->rope_npos = n;
+    }
+    *out = static_cast<const float2*>(ctx->rope_tab);
+    return B2A_OK;
 }
 
 int check_heads(b2a_context* ctx, int Hq, int Hkv) {
@@ -303,6 +333,7 @@ B2A_API int b2a_destroy(b2a_context* ctx) {
         if (ctx->pf_ws) cudaFree(ctx->pf_ws);
         if (ctx->split_ws) cudaFree(ctx->split_ws);
         if (ctx->blk_ws) cudaFree(ctx->blk_ws);
+        if (ctx->rope_tab) cudaFree(ctx->rope_tab);
     }
     delete ctx;
     return B2A_OK;
@@ -326,7 +357,7 @@ B2A_API int b2a_set_workspace_limit(b2a_context* ctx, size_t bytes) {
 
 B2A_API int b2a_workspace_bytes(const b2a_context* ctx, size_t* bytes) {
     if (!ctx || !bytes) return B2A_EINVAL;
-    *bytes = ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes + ctx->blk_ws_bytes;
+    *bytes = ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes + ctx->blk_ws_bytes + ctx->rope_tab_bytes;
     return B2A_OK;
 }
 
@@ -500,6 +531,19 @@ B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype, co
     p.causal = 1;
     p.window = window;
     p.scale = scale;
+
+    // fp32 inputs (the generic kernel) with the NeoX rotation and no rotated-key output: the
+    // kernel rotates q and k itself from the context's cached table -- one launch, no pre-pass
+    if (in_dtype == B2A_FLOAT32 && rope_mode == B2A_ROPE_NEOX && k_rot_out == nullptr) {
+        const float2* tab = nullptr;
+        if ((int64_t)pos0 + S > INT32_MAX) return fail(ctx, B2A_EINVAL, "pos0 + S exceeds the position range");
+        if ((rc = neox_table(ctx, rope_theta, D, pos0 + S, s, &tab))) return rc;
+        p.rope_table = tab;
+        p.rope_pos0 = pos0;
+        const cudaError_t e = launch_attention(ctx, p, s);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "attention kernel launch");
+        return B2A_OK;
+    }
 
     // bf16 inputs are multiplied as fp16 tensor-core operands: the rotated q/k,
     // P and V then carry 11 significant bits instead of 8, which keeps short

@@ -114,12 +114,35 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
     }
 
     // this row's query vectors, as fp32 (padding heads zero)
-    for (int g = 0; g < kHT; ++g)
-        for (int d = lane; d < D; d += 32)
-            qs[(warp * kHT + g) * D + d] =
-                row_valid && g < nh
-                    ? load_as_float(p.q, b * p.q_sb + (int64_t)s * p.q_ss + (int64_t)(h0 + g) * p.q_sh + d, p.in_dtype)
-                    : 0.f;
+    const float2* const rope = p.rope_table;
+    const int half = D >> 1;
+    if (rope != nullptr) {
+        // NeoX rotation at position rope_pos0 + s, float products from the float (cos, sin) of a
+        // double angle (INF/decoderonly/DecoderOnlyRotaryEmbedding.java:42-67)
+        const float2* cs_row = rope + (int64_t)(p.rope_pos0 + (row_valid ? s : 0)) * half;
+        for (int g = 0; g < kHT; ++g)
+            for (int i = lane; i < half; i += 32) {
+                float y0 = 0.f, y1 = 0.f;
+                if (row_valid && g < nh) {
+                    const int64_t qo = b * p.q_sb + (int64_t)s * p.q_ss + (int64_t)(h0 + g) * p.q_sh;
+                    const float a = load_as_float(p.q, qo + i, p.in_dtype);
+                    const float c = load_as_float(p.q, qo + i + half, p.in_dtype);
+                    const float2 t = __ldg(cs_row + i);
+                    y0 = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(c, t.y));
+                    y1 = __fadd_rn(__fmul_rn(a, t.y), __fmul_rn(c, t.x));
+                }
+                qs[(warp * kHT + g) * D + i] = y0;
+                qs[(warp * kHT + g) * D + i + half] = y1;
+            }
+    } else {
+        for (int g = 0; g < kHT; ++g)
+            for (int d = lane; d < D; d += 32)
+                qs[(warp * kHT + g) * D + d] =
+                    row_valid && g < nh
+                        ? load_as_float(p.q, b * p.q_sb + (int64_t)s * p.q_ss + (int64_t)(h0 + g) * p.q_sh + d,
+                                        p.in_dtype)
+                        : 0.f;
+    }
     const float sl2 = p.scale * kLog2e;
     float acc[kHT][kNPL];
     float m[kHT], l[kHT];
@@ -145,6 +168,11 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
             goff[i] = (x % G4) * 4;
         }
     }
+    // in-kernel RoPE of the staged keys: thread t rotates the pairs e = t + kRotPer * blockDim ... of a
+    // tile; with half <= 32 their (cos, sin) are fetched with the tile (no dependent load after staging)
+    constexpr int kRotPer = kTileKeys * 32 / (kRows * 32);
+    const bool rot_prefetch = kVec && rope != nullptr && half <= 32;
+    float2 trot[kRotPer];
     auto fetch = [&](int kb) {  // the tile at kb into registers (zeros past the CTA's last key)
         const int nk = min(kTileKeys, cta_last - kb + 1);
 #pragma unroll
@@ -155,6 +183,14 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
                 vraw[i] = load_raw4(p.v, r, in_dtype);
             } else {
                 kraw[i] = vraw[i] = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+        if (rot_prefetch) {
+#pragma unroll
+            for (int r = 0; r < kRotPer; ++r) {
+                const int e = (int)threadIdx.x + r * (int)blockDim.x, jj = e / half;
+                trot[r] = jj < nk ? __ldg(rope + (int64_t)(p.rope_pos0 + kb + jj) * half + (e - jj * half))
+                                  : make_float2(0.f, 0.f);
             }
         }
     };
@@ -181,6 +217,30 @@ __global__ void __launch_bounds__(kRows * 32) attn_simt_kernel(const __grid_cons
                 }
                 ks[j * Dp + d] = kv;
                 vs[j * Dp + d] = vv;
+            }
+        }
+        if (rope != nullptr) {
+            // rotate the staged keys in place at their positions (the same float rotation as q)
+            __syncthreads();
+            if (rot_prefetch) {
+#pragma unroll
+                for (int r = 0; r < kRotPer; ++r) {
+                    const int e = (int)threadIdx.x + r * (int)blockDim.x, jj = e / half, i = e - jj * half;
+                    if (jj < nk) {
+                        const float a = ks[jj * Dp + i], c = ks[jj * Dp + i + half];
+                        const float2 t = trot[r];
+                        ks[jj * Dp + i] = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(c, t.y));
+                        ks[jj * Dp + i + half] = __fadd_rn(__fmul_rn(a, t.y), __fmul_rn(c, t.x));
+                    }
+                }
+            } else {
+                for (int e = threadIdx.x; e < nk * half; e += blockDim.x) {
+                    const int jj = e / half, i = e - jj * half;
+                    const float a = ks[jj * Dp + i], c = ks[jj * Dp + i + half];
+                    const float2 t = __ldg(rope + (int64_t)(p.rope_pos0 + kb + jj) * half + i);
+                    ks[jj * Dp + i] = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(c, t.y));
+                    ks[jj * Dp + i + half] = __fadd_rn(__fmul_rn(a, t.y), __fmul_rn(c, t.x));
+                }
             }
         }
         __syncthreads();

@@ -93,6 +93,11 @@ struct AttnParams {
     const float* mask;        // additive [B][S] or NULL
     const int32_t* key_len;   // [B] or NULL
     float scale;
+    // NeoX RoPE applied inside the kernel to q and k at position rope_pos0 + s: float (cos, sin)
+    // [position][D/2] covering positions [0, rope_pos0 + S), or NULL (q and k are used as given).
+    // Only the generic kernel (attn_simt.cu) takes it.
+    const float2* rope_table;
+    int rope_pos0;
 };
 
 // Key split of the generic kernel: partial slots and per-query-block counters (zero
@@ -134,6 +139,10 @@ cudaError_t launch_rope_rows_with_table(const void* src, int src_dtype, void* ds
                                         int D, int64_t sb, int64_t ss, int64_t sh, int64_t db, int64_t ds, int64_t dh,
                                         int pos0, int rope_mode, const double* inv_freq, double2* table,
                                         bool build_table, int* status, cudaStream_t stream);
+
+// table[s][i] = float (cos, sin) of (pos0 + s) * inv_freq[i] (angles in double), s < npos.
+cudaError_t launch_rope_table_f32(float2* table, int npos, int half, int pos0, const double* inv_freq,
+                                  cudaStream_t stream);
 
 // Vectorised prefill pre-pass (D a multiple of 16, 16-byte aligned tensors):
 // each job rotates (rope_mode 1/2) or converts a dense [B][S][H][D] tensor into

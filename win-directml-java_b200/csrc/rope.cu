@@ -368,6 +368,16 @@ cudaError_t launch_rope_rows_with_table(const void* src, int src_dtype, void* ds
     return cudaGetLastError();
 }
 
+cudaError_t launch_rope_table_f32(float2* table, int npos, int half, int pos0, const double* inv_freq,
+                                  cudaStream_t stream) {
+    FreqTable f{};
+    for (int i = 0; i < half; ++i) f.inv_freq[i] = inv_freq[i];
+    const int64_t n = (int64_t)npos * half;
+    const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    rope_table_f32_kernel<<<grid, 256, 0, stream>>>(table, npos, half, pos0, f);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_convert(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n, int* status,
                            cudaStream_t stream) {
     const int64_t blocks = (n + 255) / 256;
