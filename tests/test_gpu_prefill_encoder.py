@@ -238,11 +238,30 @@ def test_prefill_rotated_keys_out_and_rope_modes(ctx, dtype, mode):
     assert np.all(np.abs(got_k - want_k) <= bound), float(np.max(np.abs(got_k - want_k) - bound))
 
 
-@pytest.mark.parametrize("layout", [0, 1])
-def test_encoder_bf16_inputs(ctx, layout):
-    lens = [100, 37, 1, 64]
-    got, want = _encoder_case(ctx, B=4, H=3, S=100, D=64, dtype=oracle.BF16, lens=lens, layout=layout, seed=600)
-    assert_close(got, want, what="bf16 encoder")
+@pytest.mark.parametrize("layout,S,D", [(0, 100, 64), (1, 100, 64), (1, 300, 32), (0, 600, 64)])
+def test_encoder_bf16_inputs(ctx, layout, S, D):
+    """bf16 encoder inputs on the tensor cores: up to 512 keys the kernel converts the staged tiles to
+    fp16 itself (its two spare warps); longer sequences go through the conversion pre-pass."""
+    lens = [S, 37, 1, 64]
+    got, want = _encoder_case(ctx, B=4, H=3, S=S, D=D, dtype=oracle.BF16, lens=lens, layout=layout, seed=600 + S)
+    assert ctx.last_attention_kernel() == "tcgen05"
+    assert_close(got, want, what=f"bf16 encoder S={S}")
+
+
+def test_encoder_bf16_beyond_the_fp16_range_is_flagged(ctx):
+    """A bf16 value beyond the fp16 operand range cannot be multiplied: the in-kernel conversion raises
+    the device status (B2A_EDEVICE), as the conversion pre-pass does."""
+    import torch
+    import b200attn
+    B, H, S, D = 1, 2, 64, 32
+    q = torch.zeros(B, S, H, D, dtype=torch.bfloat16, device="cuda")
+    q[0, 3, 1, 5] = 1e6
+    y = torch.empty(B, S, H, D, device="cuda")
+    b200attn.mha(ctx, q, q.clone(), q.clone(), y, 0.125, layout=b200attn.SEQ_MAJOR)
+    with pytest.raises(b200attn.B200RuntimeException) as ei:
+        ctx.check_device_status()
+    assert ei.value.status == b200attn.B2A_EDEVICE
+    assert "fp16 operand range" in str(ei.value)
 
 
 @pytest.mark.parametrize("dtype,window,theta,S,D", [

@@ -165,6 +165,14 @@ int neox_table(b2a_context* ctx, double theta, int D, int npos, cudaStream_t str
     return B2A_OK;
 }
 
+// Whether the tcgen05 kernel converts bf16 operands to fp16 itself instead of a pre-pass that
+// writes fp16 copies.  In the kernel two otherwise idle warps convert each staged tile, so every
+// work item converts the key/value tiles it reads: for sequences of at most 512 keys (at most two
+// work items per head) that is cheaper than the extra launch and the copies' HBM round trip; for
+// longer ones the repeated conversion costs more.  (Rotating q and k in the kernel the same way was
+// slower at every length measured, so RoPE stays in the pre-pass.)
+constexpr int kInKernelPrepMaxSeq = 512;
+
 int check_heads(b2a_context* ctx, int Hq, int Hkv) {
     // DecoderOnlyAttentionLayout constructor (INF/decoderonly/DecoderOnlyAttentionLayout.java:12-22)
     if (Hq <= 0) return fail(ctx, B2A_EINVAL, "numQueryHeads must be positive");
@@ -460,6 +468,18 @@ B2A_API int b2a_mha(b2a_context* ctx, int in_dtype, int out_dtype, const void* q
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaSuccess;
     if (in_dtype == B2A_BFLOAT16) {
+        // short sequences: the tensor-core kernel converts the staged bf16 tiles to fp16 itself
+        // (no pre-pass; measured on B200, bf16 B=64 H=12 S=128 D=32: 30.2 vs 36.3 us; S=512 D=64:
+        // 56.8 vs 69.0 us; at S=1024 D=128 the pre-pass is faster, 142 vs 151 us)
+        AttnParams t = p;
+        t.xform = 7;
+        if (S <= kInKernelPrepMaxSeq && attn_tcgen05_supported(t)) {
+            e = launch_attention(ctx, t, s);
+            if (e != cudaSuccess) return cuda_fail(ctx, e, "attention kernel launch");
+            return B2A_OK;
+        }
+    }
+    if (in_dtype == B2A_BFLOAT16) {
         // same operand rule as the prefill: bf16 inputs are multiplied as fp16
         const size_t n = (size_t)B * H * S * D;
         const size_t one = (n * 2 + 255) / 256 * 256;
@@ -532,6 +552,9 @@ B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype, co
     p.window = window;
     p.scale = scale;
 
+    const size_t nq = (size_t)B * S * Hq * D, nk = (size_t)B * S * Hkv * D;
+    auto r256 = [](size_t x) { return (x + 255) / 256 * 256; };
+
     // fp32 inputs (the generic kernel) with the NeoX rotation and no rotated-key output: the
     // kernel rotates q and k itself from the context's cached table -- one launch, no pre-pass
     if (in_dtype == B2A_FLOAT32 && rope_mode == B2A_ROPE_NEOX && k_rot_out == nullptr) {
@@ -551,8 +574,6 @@ B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype, co
     // fp16 range; values beyond it raise device status bit 2).
     const int cdt = in_dtype == B2A_BFLOAT16 ? B2A_FLOAT16 : in_dtype;
     const size_t ce = dtype_size(cdt);
-    const size_t nq = (size_t)B * S * Hq * D, nk = (size_t)B * S * Hkv * D;
-    auto r256 = [](size_t x) { return (x + 255) / 256 * 256; };
     const bool rope = rope_mode != B2A_ROPE_NONE;
     const bool conv = cdt != in_dtype;
     const size_t table_bytes = rope ? r256((size_t)S * (D / 2) * 16) : 0;

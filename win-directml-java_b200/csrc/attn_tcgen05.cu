@@ -97,11 +97,15 @@ struct TcParams {
     int fmt;  // 0 = fp16, 1 = bf16 operands
     int* sched;   // device int[2]: next work item, CTAs finished (zero between launches)
     int n_items;  // work items: query-tile pairs x heads x batch (packed: ceil(heads x batch / 2))
-    int stall;    // test hook: CTA 0 does not issue ring item 1 (its first item's V(0), K(1))
+    int stall;    // test hook: the CTA of work item 0 does not issue that item's ring item 1 (V(0), K(1))
     // packed items (bidirectional, S <= 128, two query tiles per item): tile A and tile B are the
     // single query tiles of two consecutive (batch, head) pairs, so both softmax groups work
     int packed;
+    // in-kernel operand conversion by warps 10 and 11 (kXformQ / K / V): the staged bf16 tile
+    // becomes the fp16 operand in place
+    int xform;
 };
+constexpr int kXformQ = 1, kXformK = 2, kXformV = 4;
 
 template <int D>
 struct TcGeo {
@@ -125,6 +129,46 @@ struct TcGeo {
     static constexpr uint32_t kTxTile = kTileBytes;  // bytes one K or V tile load delivers (zero fill included)
     static_assert(kBytes + 1024 <= 227 * 1024, "shared memory budget");
 };
+
+// 8 bf16 values (one 16-byte chunk) as floats (exact), and 8 floats packed to fp16.
+__device__ __forceinline__ void unpack8_bf16(uint4 r, float* x) {
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        x[2 * i] = __uint_as_float(w[i] << 16);
+        x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+__device__ __forceinline__ uint4 pack8_f16(const float* x) {
+    uint4 u;
+    u.x = pack_half2(x[0], x[1]);
+    u.y = pack_half2(x[2], x[3]);
+    u.z = pack_half2(x[4], x[5]);
+    u.w = pack_half2(x[6], x[7]);
+    return u;
+}
+
+// In-kernel conversion of one staged bf16 tile (TMA layout: 128 rows of 64-element, 128-byte-
+// swizzled panels): rows [0, rows) become fp16 in place.  Thread tx of the 64 takes rows tx and
+// tx + 64.  Returns the largest |value| (a value beyond the fp16 range becomes infinite: the
+// caller flags it).
+template <int D>
+__device__ __forceinline__ float xform_tile(unsigned char* tile, int tx, int rows) {
+    constexpr int kChunks = D / 8;  // 16-byte chunks of a row that hold data
+    float mx = 0.f;
+    for (int rr = tx; rr < rows && rr < 128; rr += 64) {
+#pragma unroll 4
+        for (int c = 0; c < kChunks; ++c) {
+            uint4* pc = reinterpret_cast<uint4*>(tile + (c >> 3) * 16384 + rr * 128 + (((c & 7) ^ (rr & 7)) << 4));
+            float x[8];
+            unpack8_bf16(*pc, x);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(x[i]));
+            *pc = pack8_f16(x);
+        }
+    }
+    return mx;
+}
 
 // 2^x on the FMA pipe instead of the MUFU: x = n + f with n = round(x) taken by adding 1.5 * 2^23 (the FP adder
 // rounds to an integer; n is then in the low mantissa bits), f in
@@ -340,7 +384,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     auto bItemFull = [&](int s) { return bar0 + 8u * (14 + 2 * ST + s); };
     auto bItemEmpty = [&](int s) { return bar0 + 8u * (16 + 2 * ST + s); };
     const uint32_t bDrain = bar0 + 8u * (18 + 2 * ST);
-    static_assert(8 * (19 + 2 * ST) <= 256, "barriers fit below the TMEM address word");
+    // in-kernel preparation: a staged tile is an MMA operand once the preparing warps release it
+    auto bQready = [&](int qs) { return bar0 + 8u * (19 + 2 * ST + qs); };
+    auto bKVready = [&](int s) { return bar0 + 8u * (23 + 2 * ST + s); };
+    static_assert(8 * (23 + 3 * ST) <= 256, "barriers fit below the TMEM address word");
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(base_ptr + Gm::oBar + 256);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(base_ptr + Gm::oBar + 264);
     // mailbox slot s: kSlotInts ints at oBar + 288 + 4 kSlotInts s, a work item's geometry
@@ -357,17 +404,20 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         for (int qs = 0; qs < Gm::kQTiles; ++qs) {
             mbar_init(bQfull(qs), 1);
             mbar_init(bQempty(qs), 1);
+            mbar_init(bQready(qs), 2);
         }
         for (int t = 0; t < 2; ++t) {
             mbar_init(bSfull(t), 1);
             mbar_init(bPfull(t), 128);
             mbar_init(bOdone(t), 1);
             mbar_init(bItemFull(t), 1);
-            mbar_init(bItemEmpty(t), 9);
+            // readers of a mailbox slot: the MMA warp, the eight softmax warps (+ the two preparing warps)
+            mbar_init(bItemEmpty(t), p.xform ? 11 : 9);
         }
         for (int s = 0; s < ST; ++s) {
             mbar_init(bKVfull(s), 1);
             mbar_init(bKVempty(s), 1);
+            mbar_init(bKVready(s), 2);
         }
         mbar_init(bDrain, 1);
         *abort_flag = 0;
@@ -397,20 +447,31 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             int k = 0;        // work items published
             int g = 0;        // ring items issued
             int q_items = 0;  // work items whose Q tiles were issued
-            const int skip_g = (p.stall && blockIdx.x == 0) ? 1 : -1;  // test hook: a copy never issued
-            // The next item's index is fetched one item ahead, and its geometry (key-length reads)
-            // before the wait for a free mailbox slot: the counter's atomic and those reads take
-            // microseconds, which would otherwise separate short items.  Packed items (uniform
-            // cost) are assigned statically: CTA c takes items c, c + grid, ...
-            int w_next = packed ? (int)blockIdx.x : atomicAdd(sched, 1);
+            int skip_g = -1;  // test hook: the ring item of work item 0 whose copy is never issued
+            // Packed items (uniform cost) are assigned statically, CTA c taking items c, c + grid, ...,
+            // and their geometry (key-length reads, microseconds under load) is computed before the wait
+            // for a free mailbox slot, so short items follow one another closely.  Other items come
+            // from the counter when the CTA is ready for one, so that no CTA holds an item it has not
+            // started while another has none.
+            int w_static = (int)blockIdx.x;
             for (;; ++k) {
-                const int w = w_next;
-                const ItemGeo it = item_geo(w < n_items ? w : 0, n_pairs, Gm::kTiles, Hq, S, causal, window, key_len,
-                                            packed, n_heads_total);
-                if (w < n_items) w_next = packed ? w + (int)gridDim.x : atomicAdd(sched, 1);
                 const int slot = k & 1;
-                // slot k % 2 is free once every reader of item k-2 is done with it
-                if (k >= 2 && !mbar_wait(bItemEmpty(slot), ((k >> 1) - 1) & 1, abort_flag, status)) break;
+                int w;
+                ItemGeo it;
+                if (packed) {
+                    w = w_static;
+                    w_static += (int)gridDim.x;
+                    it = item_geo(w < n_items ? w : 0, n_pairs, Gm::kTiles, Hq, S, causal, window, key_len, packed,
+                                  n_heads_total);
+                    // slot k % 2 is free once every reader of item k-2 is done with it
+                    if (k >= 2 && !mbar_wait(bItemEmpty(slot), ((k >> 1) - 1) & 1, abort_flag, status)) break;
+                } else {
+                    if (k >= 2 && !mbar_wait(bItemEmpty(slot), ((k >> 1) - 1) & 1, abort_flag, status)) break;
+                    w = atomicAdd(sched, 1);
+                    it = item_geo(w < n_items ? w : 0, n_pairs, Gm::kTiles, Hq, S, causal, window, key_len, packed,
+                                  n_heads_total);
+                }
+                if (p.stall && w == 0) skip_g = g + 1;
                 publish_item(slots + kSlotInts * slot, w < n_items, it, causal, window);
                 mbar_arrive(bItemFull(slot));  // release: the slot's values are visible to the waiters
                 if (w >= n_items) break;
@@ -478,6 +539,71 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             for (int i = (g > ST ? g - ST : 0); i < g; ++i)
                 if (i != skip_g) mbar_drain(bKVfull(i % ST), (i / ST) & 1);
         }
+    } else if (warp >= 10) {
+        // ------------------------------------------------------------ operand conversion
+        // Warps 10-11 follow the producer's sequence of work items and ring items: each staged bf16
+        // tile is converted to fp16 in place, made visible to the tensor core's (async) proxy, and
+        // released to the MMA warp.
+        if (p.xform != 0) {
+            const int tx = tid - 320;  // 0..63
+            const int S = p.S, xform = p.xform;
+            const bool packed = Gm::kTiles == 2 && p.packed != 0;
+            float mx = 0.f;
+            int g = 0;
+            bool ok = true;
+            auto release = [&](uint32_t bar) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar);
+            };
+            for (int k = 0; ok; ++k) {
+                const int slot = k & 1;
+                if (!__all_sync(0xffffffffu, mbar_wait(bItemFull(slot), (k >> 1) & 1, abort_flag, status))) break;
+                volatile int* const ms = slots + kSlotInts * slot;
+                if (!ms[kSlotValid]) break;
+                const int nt1 = ms[kSlotNt1], n_max = max(ms[kSlotNt0], nt1), t_begin = ms[kSlotTBegin];
+                const int qb = k % Gm::kQBuf, qpar = (k / Gm::kQBuf) & 1;
+                for (int t = 0; t < Gm::kTiles && ok; ++t) {
+                    const int qs = qb * Gm::kTiles + t;
+                    if (!__all_sync(0xffffffffu, mbar_wait(bQfull(qs), qpar, abort_flag, status))) {
+                        ok = false;
+                        break;
+                    }
+                    if (xform & kXformQ) {
+                        const int q0 = ms[t ? kSlotQ0b : kSlotQ0a];
+                        if (q0 < S && (t == 0 || nt1 > 0))
+                            mx = fmaxf(mx, xform_tile<D>(base_ptr + Gm::oQ + qs * Gm::kTileBytes, tx, S - q0));
+                    }
+                    release(bQready(qs));
+                }
+                for (int i = 0; i <= n_max && ok; ++i) {
+                    const int st = (g + i) % ST;
+                    if (!__all_sync(0xffffffffu, mbar_wait(bKVfull(st), ((g + i) / ST) & 1, abort_flag, status))) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char* const ks = base_ptr + Gm::oK + st * Gm::kTileBytes;
+                    unsigned char* const vs = base_ptr + Gm::oV + st * Gm::kTileBytes;
+                    if (packed) {
+                        // ring item 0: K tiles in both slots; ring item 1: V tiles in both
+                        if (xform & (i == 0 ? kXformK : kXformV)) {
+                            mx = fmaxf(mx, xform_tile<D>(i == 0 ? ks : vs, tx, S));
+                            if (nt1 > 0) mx = fmaxf(mx, xform_tile<D>(i == 0 ? vs : ks, tx, S));
+                        }
+                    } else {
+                        if ((xform & kXformK) && i < n_max) mx = fmaxf(mx, xform_tile<D>(ks, tx, S - (t_begin + i) * kBN));
+                        if ((xform & kXformV) && i >= 1)
+                            mx = fmaxf(mx, xform_tile<D>(vs, tx, S - (t_begin + i - 1) * kBN));
+                    }
+                    release(bKVready(st));
+                }
+                g += n_max + 1;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bItemEmpty(slot));  // done with the slot
+            }
+            // a value beyond the fp16 operand range (|x| > 65504 rounds to infinity): status bit 2
+            if (__any_sync(0xffffffffu, mx >= 65520.f) && lane == 0) atomicOr(status, 4);
+        }
     } else if (warp == 9) {
         // ------------------------------------------------------------ MMA issuer
         // The whole warp runs this loop with warp-uniform waits (vote.all); lane 0
@@ -491,9 +617,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             int item_ready = -1;      // highest ring item whose full wait was observed
             int cp0 = 0, cp1 = 0;     // P hand-overs consumed per tile
             bool ok = true;
+            // tiles prepared in kernel are operands once the preparing warps release them
+            const bool kv_prep = (p.xform & (kXformK | kXformV)) != 0, q_prep = (p.xform & kXformQ) != 0;
             auto wait_item = [&](int i) -> bool {
                 if (item_ready >= i) return true;
-                if (!__all_sync(0xffffffffu, mbar_wait(bKVfull(i % ST), (i / ST) & 1, abort_flag, status)))
+                if (!__all_sync(0xffffffffu, mbar_wait(kv_prep ? bKVready(i % ST) : bKVfull(i % ST), (i / ST) & 1,
+                                                       abort_flag, status)))
                     return false;
                 tc_fence_after();
                 item_ready = i;
@@ -544,8 +673,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 const int nt0 = ms[kSlotNt0], nt1 = ms[kSlotNt1], n_max = max(nt0, nt1);
                 qb = k % Gm::kQBuf;
                 const int qpar = (k / Gm::kQBuf) & 1, qs0 = qb * Gm::kTiles;
-                ok = __all_sync(0xffffffffu, mbar_wait(bQfull(qs0), qpar, abort_flag, status) &&
-                                                 (Gm::kTiles == 1 || mbar_wait(bQfull(qs0 + 1), qpar, abort_flag, status)));
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait(q_prep ? bQready(qs0) : bQfull(qs0), qpar, abort_flag, status) &&
+                                    (Gm::kTiles == 1 ||
+                                     mbar_wait(q_prep ? bQready(qs0 + 1) : bQfull(qs0 + 1), qpar, abort_flag, status)));
                 if (ok) ok = wait_item(g);
                 if (!ok) break;
                 // S_t(0); a tile with at most one key tile reads Q_t for the last time here
@@ -880,6 +1011,7 @@ cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream, b
     p.n_items = (int)work_items(a);
     p.stall = stall ? 1 : 0;
     p.packed = packed_items(a) ? 1 : 0;
+    p.xform = a.xform;
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
                                                   cudaSuccess || sms <= 0)
@@ -895,8 +1027,10 @@ cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream, b
 }  // namespace
 
 bool attn_tcgen05_supported(const AttnParams& p) {
-    // fp16 operands only: P goes to TMEM as fp16 and both MMA operands share one type
-    if (p.in_dtype != kF16) return false;
+    // fp16 operands only: P goes to TMEM as fp16 and both MMA operands share one type; bf16 inputs
+    // are converted by the kernel itself when it prepares all three tensors (xform 7)
+    if (p.in_dtype != kF16 && !(p.in_dtype == kBF16 && p.xform == 7)) return false;
+    if (p.in_dtype == kF16 && p.xform != 0) return false;
     if (!(p.D == 32 || p.D == 64 || p.D == 96 || p.D == 128 || p.D == 256)) return false;
     const int64_t strides[] = {p.q_sb, p.q_ss, p.q_sh, p.k_sb, p.k_ss, p.k_sh};
     for (int64_t s : strides)

@@ -98,6 +98,9 @@ struct AttnParams {
     // Only the generic kernel (attn_simt.cu) takes it.
     const float2* rope_table;
     int rope_pos0;
+    // tcgen05 kernel only: 7 = q, k and v are bf16 (in_dtype) and the kernel converts each staged
+    // tile to fp16 in shared memory; 0 = fp16 operands as given.
+    int xform;
 };
 
 // Key split of the generic kernel: partial slots and per-query-block counters (zero
@@ -127,7 +130,7 @@ constexpr int kStatusBufferInts = 8;
 // tcgen05 / TMEM / TMA kernel (fp16 operands, head_dim 64, 96, 128); status bit 3 = bounded wait ran out.
 // `status` is the context's status buffer (kStatusBufferInts ints).
 bool attn_tcgen05_supported(const AttnParams& p);
-// stall (test hook): CTA 0 leaves one K/V copy of its first work item unissued, so a
+// stall (test hook): the CTA that takes work item 0 leaves one of its K/V copies unissued, so a
 // bounded wait runs out (status bit 3).
 cudaError_t launch_attn_tcgen05(const AttnParams& p, int* status, cudaStream_t stream, bool stall = false);
 bool attn_tc_supported(const AttnParams& p);
