@@ -73,3 +73,12 @@ def test_group_with_a_bad_rank_count_is_b2a_enccl():
         b200attn.Group([])
     assert ei.value.status == b200attn.B2A_ENCCL
     assert "ncclCommInitAll(0 ranks)" in str(ei.value)
+
+
+def test_catalog_backend_has_cuda_with_its_token():
+    from b200attn.catalog import CatalogBackend
+    assert [b.token() for b in CatalogBackend] == ["cpu", "directml", "warp", "auto", "cuda"]
+    assert CatalogBackend.parse("cuda") is CatalogBackend.CUDA
+    assert CatalogBackend.parse(" CUDA ") is CatalogBackend.CUDA
+    with pytest.raises(ValueError):
+        CatalogBackend.parse("metal")
