@@ -288,21 +288,45 @@ class DecodeWorkload:
         for i in range(len(self.layers)):
             self.launch(ctx, i, stream)
 
-    def step_e2e(self, ctx, stream=None):
-        self.lens_d.copy_(self.h_lens, non_blocking=True)
+    def step_e2e(self, ctx):
+        """One step through the public API with its host transfers: the step's inputs (new q/k/v
+        rows, context lengths) from pinned host memory, the outputs back to pinned host memory.
+        Copies run on a copy stream: layer 1's inputs arrive while layer 0 computes and layer 0's
+        outputs leave while layer 1 computes.  The step ends when its last copy has landed (the
+        next step's inputs depend on this step's outputs in a real decode loop)."""
+        torch = self.torch
+        main = torch.cuda.current_stream()
+        if not hasattr(self, "copy_stream"):
+            self.copy_stream = torch.cuda.Stream()
+            self.ev_in = [torch.cuda.Event() for _ in self.layers]
+            self.ev_out = [torch.cuda.Event() for _ in self.layers]
+            self.ev_done = torch.cuda.Event()
+        cs = self.copy_stream
+        cs.wait_stream(main)  # the previous step (and its copies) is complete
+        with torch.cuda.stream(cs):
+            self.lens_d.copy_(self.h_lens, non_blocking=True)
+            for i in range(len(self.layers)):
+                self.q[i].copy_(self.h_q[i], non_blocking=True)
+                self.kn[i].copy_(self.h_kn[i], non_blocking=True)
+                self.vn[i].copy_(self.h_vn[i], non_blocking=True)
+                self.ev_in[i].record(cs)
         for i in range(len(self.layers)):
-            self.q[i].copy_(self.h_q[i], non_blocking=True)
-            self.kn[i].copy_(self.h_kn[i], non_blocking=True)
-            self.vn[i].copy_(self.h_vn[i], non_blocking=True)
-            self.launch(ctx, i, stream)
+            main.wait_event(self.ev_in[i])
+            self.launch(ctx, i)
+            self.ev_out[i].record(main)
             if self.world == 1:
-                self.h_out[i].copy_(self.out[i], non_blocking=True)
+                cs.wait_event(self.ev_out[i])
+                with torch.cuda.stream(cs):
+                    self.h_out[i].copy_(self.out[i], non_blocking=True)
         if self.world > 1:
             # output reassembly: one NCCL all-gather of the equal shards (both layers at once),
             # scattered back into unit order, then the whole batch's outputs to the host
-            local = self.torch.stack(self.out, dim=1)  # [units, layers, G, D]
+            local = torch.stack(self.out, dim=1)  # [units, layers, G, D]
             full = self.reassemble(local)
             self.h_out_all.copy_(full.transpose(0, 1), non_blocking=True)
+        else:
+            self.ev_done.record(cs)
+            main.wait_event(self.ev_done)
 
     def e2e_bytes(self):
         h2d = self.lens.nbytes + sum(t.numel() * t.element_size() for t in self.h_q + self.h_kn + self.h_vn)
