@@ -46,6 +46,8 @@ WORKLOADS = {
     "c3": "Qwen2.5-0.5B decode B64 14/2 D64 fp16 KV ctx~U[512,8192] (configs[2])",
     "c4": "Phi-3-mini causal prefill B8 S4096 H32 D96 bf16 (configs[3])",
     "c5": "Gemma-3-270M decode B256 4/1 D256 local W512 + global, QK-norm, fp16 KV ctx~U[1024,32768] (configs[4])",
+    "c3blk": "Qwen2.5-0.5B decode attention block B64 hidden 896 14/2 D64 fp16: QKV GEMM + bias, decode, "
+             "O GEMM + residual (configs[2] with its projections)",
 }
 
 
@@ -393,6 +395,56 @@ class PrefillWorkload:
                                     rope_theta=self.theta, stream=stream)
 
 
+class BlockWorkload:
+    """c3blk: configs[2]'s decode step with the projections around it (b2a_decode_attention_block):
+    x [64, 896] -> QKV GEMM (+bias) -> fused decode (RoPE, append, GQA attention) -> O GEMM
+    (+residual); random weights of Qwen2.5-0.5B's shapes (no checkpoint)."""
+
+    def __init__(self, seed: int = 3):
+        import torch
+        import b200attn
+        from b200attn import synthetic
+        self.torch, self.b2a = torch, b200attn
+        self.B, self.hidden, self.Hq, self.Hkv, self.D, self.max_seq = 64, 896, 14, 2, 64, 8193
+        self.lens = synthetic.uniform_int(seed, self.B, 512, 8192)
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        nqkv = (self.Hq + 2 * self.Hkv) * self.D
+        w = lambda *sh: (torch.randn(*sh, generator=g, device="cuda") / math.sqrt(sh[-1])).half()
+        self.x = torch.randn(self.B, self.hidden, generator=g, device="cuda").half()
+        self.res = torch.randn(self.B, self.hidden, generator=g, device="cuda").half()
+        self.wqkv, self.wo = w(nqkv, self.hidden), w(self.hidden, self.Hq * self.D)
+        self.bqkv = 0.1 * torch.randn(nqkv, generator=g, device="cuda")
+        shape = (self.B, self.Hkv, self.max_seq, self.D)
+        self.kc = torch.empty(shape, dtype=torch.float16, device="cuda")
+        self.vc = torch.empty(shape, dtype=torch.float16, device="cuda")
+        for t in (self.kc, self.vc):
+            for b in range(self.B):
+                t[b].normal_(generator=g)
+        self.lens_d = torch.from_numpy(self.lens).cuda()
+        self.y = torch.empty(self.B, self.hidden, dtype=torch.float16, device="cuda")
+
+    def tokens_per_step(self):
+        return self.B
+
+    def kernel_launches_per_step(self):
+        return 3
+
+    def algorithmic_bytes(self):
+        kv = int((self.lens.astype(np.int64) + 1).sum()) * self.Hkv * self.D * 2 * 2
+        weights = (self.wqkv.numel() + self.wo.numel()) * 2
+        act = self.B * self.hidden * 2 * 3 + self.B * self.Hkv * self.D * 2 * 2
+        return kv + weights + act
+
+    def flops(self):
+        proj = 2 * self.B * self.hidden * (self.wqkv.shape[0] + self.Hq * self.D)
+        return proj + int((self.lens.astype(np.int64) + 1).sum()) * self.Hq * self.D * 4
+
+    def step(self, ctx, stream=None):
+        self.b2a.decode_attention_block(ctx, self.x, self.wqkv, self.bqkv, self.kc, self.vc, self.lens_d, self.wo,
+                                        self.res, self.y, num_q_heads=self.Hq, num_kv_heads=self.Hkv, scale=0.125,
+                                        rope_theta=1e6, stream=stream)
+
+
 def capture_graph(torch, fn):
     """CUDA graph of fn(), which launches its work on the current stream (the library
     calls take torch's current stream), or None when capture is not possible.  Replaying
@@ -444,8 +496,9 @@ def run_suite(ctx, hbm, tflops, src):
         flush_buf.fill_(1.0)
         torch.sum(clean_buf, dim=0, out=clean_sum)
     out = {}
-    for name in ("c1", "c2", "c3", "c4"):
-        w = DecodeWorkload(name, 3) if name == "c3" else PrefillWorkload(name, {"c1": 1, "c2": 2, "c4": 4}[name])
+    for name in ("c1", "c2", "c3", "c4", "c3blk"):
+        w = DecodeWorkload(name, 3) if name == "c3" else BlockWorkload() if name == "c3blk" else \
+            PrefillWorkload(name, {"c1": 1, "c2": 2, "c4": 4}[name])
         for _ in range(3):
             w.step(ctx)
         torch.cuda.synchronize()
@@ -606,8 +659,13 @@ def main():
     ctx = b200attn.Context(local)
     hbm, tflops, src = peaks()
 
-    w = DecodeWorkload(args.workload, 5, args.batch, world, rank) if args.workload in ("c3", "c5") else \
-        PrefillWorkload(args.workload, {"c1": 1, "c2": 2, "c4": 4}[args.workload], args.batch)
+    if args.workload == "c3blk":
+        if world > 1:
+            raise SystemExit("--workload c3blk runs on one GPU")
+        w = BlockWorkload()
+    else:
+        w = DecodeWorkload(args.workload, 5, args.batch, world, rank) if args.workload in ("c3", "c5") else \
+            PrefillWorkload(args.workload, {"c1": 1, "c2": 2, "c4": 4}[args.workload], args.batch)
     for _ in range(args.warmup):
         w.step(ctx)
     torch.cuda.synchronize()
@@ -692,6 +750,12 @@ def main():
                 "bytes_per_step": w.algorithmic_bytes(), "traffic": None,
                 "per_layer_ms": [round(statistics.mean(per_launch[i::len(w.layers)]), 4)
                                  for i in range(len(w.layers))]}
+    elif isinstance(w, BlockWorkload):
+        achieved = w.algorithmic_bytes() * args.steps / (kern_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "peak_source": src + " (hbm_gbs, burst copy)",
+                "kernel": "decode_tc_kernel<64,half> + linear_tc_kernel<128>", "bytes_per_step": w.algorithmic_bytes(),
+                "traffic": None}
     else:
         achieved = w.flops() * args.steps / (kern_ms / 1e3) / 1e12
         roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tflops, "unit": "TFLOP/s",
@@ -713,7 +777,8 @@ def main():
     line = {"metric": "decode tokens/s" if isinstance(w, DecodeWorkload) else "attn tokens/s",
             "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16" if isinstance(w, DecodeWorkload) else str(w.dt).split(".")[-1],
+            "vs_baseline": None,
+            "dtype": "f16" if isinstance(w, (DecodeWorkload, BlockWorkload)) else str(w.dt).split(".")[-1],
             "data": "synthetic (seeded N(0,1); no dataset or checkpoint)",
             "config": dict(w.config() if isinstance(w, DecodeWorkload) else {"workload": WORKLOADS[args.workload]},
                            parallelism=f"shard{world} (sequences per rank)", launch=launch_mode),
