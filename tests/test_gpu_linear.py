@@ -29,6 +29,7 @@ def _gemm(x, w, bias=None, residual=None):
     (64, 896, 896, oracle.BF16, oracle.BF16, False, True),   # O projection + residual, bf16
     (300, 200, 136, oracle.F16, oracle.F16, True, True),     # ragged M, N and a K that is not a multiple of 64
     (1, 72, 8, oracle.BF16, oracle.F32, False, False),       # one row, the smallest K
+    (1024, 2048, 192, oracle.F16, oracle.F16, True, True),   # enough output tiles to fill the GPU: no split-K
 ])
 def test_linear_matches_float64(ctx, M, N, K, dtype, out_dtype, use_bias, use_res):
     import torch
@@ -49,6 +50,25 @@ def test_linear_matches_float64(ctx, M, N, K, dtype, out_dtype, use_bias, use_re
                                                                          else 2.0 ** -11)
     assert np.all(np.isfinite(got))
     assert np.all(np.abs(got - want) <= tol), float(np.max(np.abs(got - want) - tol))
+
+
+def test_linear_split_k_shapes_back_to_back(ctx):
+    """Decode-shaped projections split K over CTAs and meet in an fp32 accumulator that each tile's last
+    CTA leaves at zero: launches of different shapes, queued without a synchronisation, must each be right."""
+    import torch
+    import b200attn
+    runs = []
+    for i, (M, N, K) in enumerate([(64, 1152, 896), (64, 896, 896), (8, 300, 2048), (64, 1152, 896)]):
+        x = normal(950 + i, (M, K), oracle.F16)
+        w = oracle.round_to(normal(960 + i, (N, K), oracle.F32) / math.sqrt(K), oracle.F16)
+        bias = normal(970 + i, (N,), oracle.F32)
+        y = torch.full((M, N), float("nan"), device="cuda")
+        b200attn.linear(ctx, to_dev(x, oracle.F16), to_dev(w, oracle.F16), y, bias=torch.from_numpy(bias).cuda())
+        runs.append((y, _gemm(x, w, bias)))
+    torch.cuda.synchronize()
+    ctx.check_device_status()
+    for i, (y, want) in enumerate(runs):
+        assert np.max(np.abs(to_np(y) - want)) < 1e-4, i
 
 
 def test_linear_residual_in_place(ctx):

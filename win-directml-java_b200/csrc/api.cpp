@@ -46,6 +46,10 @@ struct b2a_context {
     // attention block: the QKV projection's fp32 rows and the attention output
     void* blk_ws = nullptr;
     size_t blk_ws_bytes = 0;
+    // split-K projections: [tile counters][fp32 accumulator], all zero between launches
+    void* lin_ws = nullptr;
+    size_t lin_ws_bytes = 0;
+    size_t lin_region = 0;
     // generic-kernel key split: [counters][partial slots], the same layout rules as dec_ws
     void* split_ws = nullptr;
     size_t split_ws_bytes = 0;
@@ -98,7 +102,8 @@ size_t dtype_size(int d) { return d == B2A_FLOAT32 ? 4 : 2; }
 int ensure_buffer(b2a_context* ctx, void** buf, size_t* have, size_t need, const char* what) {
     if (*have >= need) return B2A_OK;
     const size_t other =
-        ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes + ctx->blk_ws_bytes + ctx->rope_tab_bytes - *have;
+        ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes + ctx->blk_ws_bytes + ctx->rope_tab_bytes +
+        ctx->lin_ws_bytes - *have;
     if (ctx->ws_limit != 0 && need + other > ctx->ws_limit)
         return fail(ctx, B2A_EOOM, "%s workspace of %zu bytes exceeds the context limit of %zu bytes", what,
                     need + other, ctx->ws_limit);
@@ -342,6 +347,7 @@ B2A_API int b2a_destroy(b2a_context* ctx) {
         if (ctx->split_ws) cudaFree(ctx->split_ws);
         if (ctx->blk_ws) cudaFree(ctx->blk_ws);
         if (ctx->rope_tab) cudaFree(ctx->rope_tab);
+        if (ctx->lin_ws) cudaFree(ctx->lin_ws);
     }
     delete ctx;
     return B2A_OK;
@@ -365,7 +371,8 @@ B2A_API int b2a_set_workspace_limit(b2a_context* ctx, size_t bytes) {
 
 B2A_API int b2a_workspace_bytes(const b2a_context* ctx, size_t* bytes) {
     if (!ctx || !bytes) return B2A_EINVAL;
-    *bytes = ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes + ctx->blk_ws_bytes + ctx->rope_tab_bytes;
+    *bytes = ctx->dec_ws_bytes + ctx->pf_ws_bytes + ctx->split_ws_bytes + ctx->blk_ws_bytes + ctx->rope_tab_bytes +
+             ctx->lin_ws_bytes;
     return B2A_OK;
 }
 
@@ -964,6 +971,25 @@ B2A_API int b2a_linear(b2a_context* ctx, int in_dtype, int out_dtype, const void
     a.M = M;
     a.N = N;
     a.K = K;
+    a.ksplit = 1;
+    // launches with too few output tiles to fill the GPU split K over CTAs (without room for the
+    // split workspace under the context's limit they run unsplit)
+    size_t acc_bytes = 0, counter_ints = 0;
+    const int ks = linear_split_plan(M, N, K, ctx->sm_count, &acc_bytes, &counter_ints);
+    if (ks > 1) {
+        // the accumulator counts as counter region: zeroed when new or grown, kept zero by the kernel
+        const size_t region_ints = counter_ints + (acc_bytes + sizeof(int) - 1) / sizeof(int) + 64;
+        size_t region_bytes = 0;
+        if (ensure_counted_buffer(ctx, &ctx->lin_ws, &ctx->lin_ws_bytes, &ctx->lin_region, region_ints, 0,
+                                  "projection split workspace", static_cast<cudaStream_t>(stream), false,
+                                  &region_bytes) == B2A_OK) {
+            a.ksplit = ks;
+            a.counters = static_cast<int*>(ctx->lin_ws);
+            a.acc = reinterpret_cast<float*>(static_cast<char*>(ctx->lin_ws) + (counter_ints * sizeof(int) + 255) / 256 * 256);
+        } else {
+            ctx->last_error.clear();  // the refused workspace is not an error of this call
+        }
+    }
     const cudaError_t e = launch_linear_tc(a, ctx->status, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(ctx, e, "linear kernel launch");
     return B2A_OK;

@@ -188,8 +188,15 @@ struct LinearArgs {
     int64_t ldy;
     int out_dtype;
     int M, N, K;
+    // split-K (linear_split_plan): ksplit K ranges per output tile, an fp32 [M][N] accumulator and
+    // per-tile counters, both zero between launches
+    int ksplit;
+    float* acc;
+    int* counters;
 };
 bool linear_tc_supported(int in_dtype, int K, int64_t ldx, int64_t ldw, const void* x, const void* w);
+// K ranges per output tile for a launch that leaves SMs idle (1: no split), and its workspace.
+int linear_split_plan(int M, int N, int K, int sm_count, size_t* acc_bytes, size_t* counter_ints);
 cudaError_t launch_linear_tc(const LinearArgs& a, int* status, cudaStream_t stream);
 
 // Sets the message b2a_last_error(NULL, ...) returns on this thread.

@@ -3,7 +3,7 @@
 // into the GEMM epilogue (the QKV projection's bias, the O projection's residual
 // add; INF/qwen/Qwen2Runtime.java:693-716 / 888-914 and 756-777 / 973-1000).
 //
-// CTA = one 128-row x BN-column output tile, 128 threads:
+// CTA = one 128-row x BN-column output tile (and, split-K, one range of its K panels), 128 threads:
 //   warp 0, lane 0  TMA producer: x and W tiles of 64 K-columns (128-byte swizzle)
 //                   into a 4-stage ring;
 //   warp 1          MMA issuer (lane 0 issues): per K panel four
@@ -13,11 +13,18 @@
 //                   the bias and the residual to its accumulator row.
 // Rows past M and K columns past K are zero-filled by the TMA loads; columns past
 // N are not stored.  Every mbarrier wait is bounded (status bit 3 on a timeout).
+// Split-K (launches with too few output tiles to fill the GPU, e.g. decode projections with
+// M = batch <= 128): the K panels are cut into ksplit ranges, one CTA each; each CTA adds its
+// partial tile into an fp32 accumulator (vector atomics), and the tile's last CTA (a per-tile
+// counter) adds bias and residual, stores y, and leaves the accumulator rows and the counter at
+// zero for the next launch.  The accumulation order, and so the last bits of y, may differ
+// between runs.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -52,9 +59,22 @@ struct LinParams {
     int out_dtype;
     int fmt;               // MMA operand type: 0 fp16, 1 bf16
     int* status;
+    int ksplit;            // K ranges per output tile (1: no split)
+    int panels_per_split;  // K panels (64 columns) per range
+    float* acc;            // split-K: fp32 [M][N] accumulator, zero between launches
+    int* counters;         // split-K: [tiles], zero between launches
 };
 
 __device__ __forceinline__ float lin_load(const void* p, int64_t i, int dtype) { return load_as_float(p, i, dtype); }
+
+// Fire-and-forget fp32 adds in L2 (red, no value returned): four consecutive floats (16-byte aligned) or one.
+__device__ __forceinline__ void red_add4(float* a, float x, float y, float z, float w) {
+    asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(a), "f"(x), "f"(y), "f"(z), "f"(w)
+                 : "memory");
+}
+__device__ __forceinline__ void red_add1(float* a, float x) {
+    asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(a), "f"(x) : "memory");
+}
 
 template <int BN>
 __global__ void __launch_bounds__(kLThreads, 1)
@@ -71,12 +91,15 @@ __global__ void __launch_bounds__(kLThreads, 1)
     const uint32_t bDrain = bar0 + 8u * (2 * kLStages + 1);
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(base_ptr + Gm::oBar + 128);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(base_ptr + Gm::oBar + 136);
+    volatile int* last_flag = reinterpret_cast<volatile int*>(base_ptr + Gm::oBar + 140);  // split-K
     auto sX = [&](int s) { return base + (uint32_t)(s * Gm::kStage); };
     auto sW = [&](int s) { return base + (uint32_t)(s * Gm::kStage + Gm::kATile); };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     int* const status = p.status;
-    const int nk = (p.K + kLBK - 1) / kLBK;
+    const int nk_all = (p.K + kLBK - 1) / kLBK;
+    const int kt0 = (int)blockIdx.z * p.panels_per_split;
+    const int nk = min(nk_all, kt0 + p.panels_per_split) - kt0;  // this CTA's K panels: kt0 .. kt0 + nk - 1
     const int m0 = blockIdx.x * kLBM, n0 = blockIdx.y * BN;
 
     if (tid == 0) {
@@ -108,8 +131,8 @@ __global__ void __launch_bounds__(kLThreads, 1)
                 const int st = kt % kLStages;
                 if (kt >= kLStages && !mbar_wait(bEmpty(st), ((kt / kLStages) - 1) & 1, abort_flag, status)) break;
                 mbar_expect_tx(bFull(st), Gm::kStage);
-                tma_load_2d(sX(st), &tmX, bFull(st), kt * kLBK, m0);
-                tma_load_2d(sW(st), &tmW, bFull(st), kt * kLBK, n0);
+                tma_load_2d(sX(st), &tmX, bFull(st), (kt0 + kt) * kLBK, m0);
+                tma_load_2d(sW(st), &tmW, bFull(st), (kt0 + kt) * kLBK, n0);
                 issued = kt + 1;
             }
             // every copy issued lands before the CTA may exit
@@ -139,13 +162,56 @@ __global__ void __launch_bounds__(kLThreads, 1)
     }
 
     // ---------------------------------------------------------------- epilogue
+    // Thread t reads TMEM lane t (output row t), 32 columns at a time.  Split-K launches stage each
+    // chunk in shared memory and walk it row-major, four columns per thread, so that the reductions
+    // and the final pass are coalesced (eight threads cover a 128-byte row segment).
     __syncwarp();
     const bool ok = __all_sync(0xffffffffu, mbar_wait(bDone, 0, abort_flag, status));
     tc_fence_after();
-    if (ok) {
-        const int row = warp * 32 + lane;
-        const int m = m0 + row;
+    constexpr int kPitch = 36;  // staged row pitch (floats): 16-byte aligned, conflict-free float4 writes
+    float* const stage = reinterpret_cast<float*>(base_ptr);  // the ring is idle once every MMA is done
+    const int rows = min(kLBM, p.M - m0);
+    const bool vec_y = (p.ldy % 4 == 0) && (p.residual == nullptr || p.ldr % 4 == 0);
+    // bias, residual and the store of 4 consecutive columns n .. n+3 (cnt of them valid) of row m
+    auto finish4 = [&](int m, int n, float4 v, int cnt) {
+        float x[4] = {v.x, v.y, v.z, v.w};
+        if (p.bias != nullptr) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (e < cnt) x[e] += __ldg(p.bias + n + e);
+        }
+        if (p.residual != nullptr) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (e < cnt) x[e] += lin_load(p.residual, (int64_t)m * p.ldr + n + e, p.out_dtype);
+        }
+        const int64_t off = (int64_t)m * p.ldy + n;
+        if (cnt == 4 && vec_y) {
+            if (p.out_dtype == kF32) {
+                *reinterpret_cast<float4*>(static_cast<float*>(p.y) + off) = make_float4(x[0], x[1], x[2], x[3]);
+            } else {
+                uint2 u;
+                if (p.out_dtype == kF16) {
+                    u.x = pack_half2(x[0], x[1]);
+                    u.y = pack_half2(x[2], x[3]);
+                } else {
+                    __nv_bfloat162 a = __floats2bfloat162_rn(x[0], x[1]), b = __floats2bfloat162_rn(x[2], x[3]);
+                    u.x = *reinterpret_cast<uint32_t*>(&a);
+                    u.y = *reinterpret_cast<uint32_t*>(&b);
+                }
+                *reinterpret_cast<uint2*>(static_cast<unsigned short*>(p.y) + off) = u;
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (e < cnt) store_from_float(p.y, off + e, x[e], p.out_dtype);
+        }
+    };
+    if (ok && p.ksplit == 1) {
+        // one output tile per CTA: each thread stores its own row (16-byte stores); a CTA-wide staging
+        // pass would add two barriers per 32 columns to every tile of a large GEMM
         const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        const int m = m0 + warp * 32 + lane;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
             uint32_t r[32];
@@ -176,6 +242,73 @@ __global__ void __launch_bounds__(kLThreads, 1)
                 for (int e = 0; e < 32; ++e)
                     if (e < cnt) store_from_float(p.y, off + e, v[e], p.out_dtype);
             }
+        }
+    } else if (ok) {
+        // split-K: the partial tile goes through the staging tile so that its vector reductions into
+        // the accumulator are coalesced
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        const int row = warp * 32 + lane;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            const int nc = n0 + 32 * c;
+            if (nc >= p.N) break;  // uniform across the CTA
+            uint32_t r[32];
+            tmem_ld32(lane_base + 32 * c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; e += 4)
+                *reinterpret_cast<float4*>(stage + row * kPitch + e) =
+                    make_float4(__uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]),
+                                __uint_as_float(r[e + 3]));
+            __syncthreads();
+            const int cols = min(32, p.N - nc);
+            for (int idx = tid; idx < rows * 8; idx += kLThreads) {
+                const int rr = idx >> 3, c4 = (idx & 7) * 4;
+                if (c4 >= cols) continue;
+                const float4 v = *reinterpret_cast<const float4*>(stage + rr * kPitch + c4);
+                const int m = m0 + rr, n = nc + c4, cnt = min(4, cols - c4);
+                float* a = p.acc + (int64_t)m * p.N + n;
+                if (cnt == 4 && ((uintptr_t)a & 15) == 0) {
+                    red_add4(a, v.x, v.y, v.z, v.w);
+                } else {
+                    const float x[4] = {v.x, v.y, v.z, v.w};
+                    for (int e = 0; e < cnt; ++e) red_add1(a + e, x[e]);
+                }
+            }
+            __syncthreads();  // the staging tile is rewritten by the next chunk
+        }
+    }
+    if (p.ksplit > 1) {
+        // the tile's last range to finish completes it: bias, residual, store, and the accumulator
+        // rows and the counter back to zero
+        __threadfence();
+        __syncthreads();
+        int* const counter = p.counters + blockIdx.y * gridDim.x + blockIdx.x;
+        if (tid == 0) *last_flag = atomicAdd(counter, 1) == p.ksplit - 1;
+        __syncthreads();
+        if (*last_flag) {
+            __threadfence();
+            const int cols = min(BN, p.N - n0);
+            const int c4n = (cols + 3) / 4;
+            for (int idx = tid; idx < rows * c4n; idx += kLThreads) {
+                const int rr = idx / c4n, c4 = (idx - rr * c4n) * 4;
+                const int m = m0 + rr, n = n0 + c4, cnt = min(4, cols - c4);
+                float* a = p.acc + (int64_t)m * p.N + n;
+                float4 v;
+                if (cnt == 4 && ((uintptr_t)a & 15) == 0) {
+                    v = __ldcg(reinterpret_cast<const float4*>(a));
+                    *reinterpret_cast<float4*>(a) = make_float4(0.f, 0.f, 0.f, 0.f);
+                } else {
+                    float x[4] = {0.f, 0.f, 0.f, 0.f};
+                    for (int e = 0; e < cnt; ++e) {
+                        x[e] = __ldcg(a + e);
+                        a[e] = 0.f;
+                    }
+                    v = make_float4(x[0], x[1], x[2], x[3]);
+                }
+                finish4(m, n, v, cnt);
+            }
+            if (tid == 0) *counter = 0;
         }
     }
     // all MMAs this CTA issued are complete before TMEM is released
@@ -223,6 +356,18 @@ bool linear_tc_supported(int in_dtype, int K, int64_t ldx, int64_t ldw, const vo
     return encode_fn() != nullptr;
 }
 
+int linear_split_plan(int M, int N, int K, int sm_count, size_t* acc_bytes, size_t* counter_ints) {
+    const int tiles = ((M + kLBM - 1) / kLBM) * ((N + kLinBN - 1) / kLinBN);
+    const int nk = (K + kLBK - 1) / kLBK;
+    int ks = 1;
+    if (2 * tiles <= sm_count) ks = std::min(nk, std::max(1, sm_count / tiles));
+    const int pps = (nk + ks - 1) / ks;
+    ks = (nk + pps - 1) / pps;  // no empty ranges
+    *acc_bytes = ks > 1 ? (size_t)M * N * sizeof(float) : 0;
+    *counter_ints = ks > 1 ? (size_t)tiles : 0;
+    return ks;
+}
+
 cudaError_t launch_linear_tc(const LinearArgs& a, int* status, cudaStream_t stream) {
     const cudaError_t ready = linear_ready();
     if (ready != cudaSuccess) return ready;
@@ -242,7 +387,12 @@ cudaError_t launch_linear_tc(const LinearArgs& a, int* status, cudaStream_t stre
     p.out_dtype = a.out_dtype;
     p.fmt = fmt;
     p.status = status;
-    const dim3 grid((unsigned)((a.M + kLBM - 1) / kLBM), (unsigned)((a.N + kLinBN - 1) / kLinBN));
+    const int nk = (a.K + kLBK - 1) / kLBK;
+    p.ksplit = a.ksplit > 1 ? a.ksplit : 1;
+    p.panels_per_split = (nk + p.ksplit - 1) / p.ksplit;
+    p.acc = a.acc;
+    p.counters = a.counters;
+    const dim3 grid((unsigned)((a.M + kLBM - 1) / kLBM), (unsigned)((a.N + kLinBN - 1) / kLinBN), (unsigned)p.ksplit);
     linear_tc_kernel<kLinBN><<<grid, kLThreads, LinGeo<kLinBN>::kBytes + 1024, stream>>>(mx, mw, p);
     return cudaGetLastError();
 }
