@@ -106,9 +106,6 @@ __device__ __forceinline__ bool seq_range_of(const DecodeParams& p, int L_in, in
     else first = 0;
     return true;
 }
-__device__ __forceinline__ bool seq_range(const DecodeParams& p, int b, int& L, int& first) {
-    return seq_range_of(p, ctx_len_of(p, b), L, first);
-}
 
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
@@ -301,6 +298,10 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
     const long long range_hi =
         aligned ? (blockIdx.x + 1) * n_units / n_cta * unit_len : min(total, range_lo + R);
 
+    // Where shared memory holds no copy of the lengths (head dim 256), the next sequence's
+    // length is requested one piece ahead: a global read made when the piece needs it
+    // waits behind the other CTAs' streams for about a microsecond.
+    int pf_b = -1, pf_len = 0;
     for (long long pos = range_lo; pos < range_hi;) {
         // unit containing pos: sequence b (prefix search), then (kv head, head group)
         int lo = 0, hi = p.B - 1;
@@ -310,8 +311,18 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
             else hi = mid - 1;
         }
         const int b = lo;
+        int L_in;
+        if (Gm::kLensCached) {
+            L_in = lens_s[b];
+        } else {
+            L_in = b == pf_b ? pf_len : ctx_len_of(p, b);
+            if (b + 1 < p.B) {
+                pf_b = b + 1;
+                pf_len = ctx_len_of(p, b + 1);  // used by the next piece, if it is in sequence b + 1
+            }
+        }
         int L, first;
-        const bool ok = seq_range_of(p, Gm::kLensCached ? lens_s[b] : ctx_len_of(p, b), L, first);
+        const bool ok = seq_range_of(p, L_in, L, first);
         const int n_b = L - first + 1;
         const int n_v = n_b + Gm::kGapKeys;  // the unit's stream length
         const long long seq_base = (long long)prefix[b] * per_chunk;
@@ -559,14 +570,19 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
             l1 += __shfl_xor_sync(0xffffffffu, l1, o);
         }
         {
+            // The warp's unnormalised O as [d][head] float pairs (heads 2t, 2t+1 of row d),
+            // the head index XOR-swizzled by (d >> 2) & 7: these pair stores and the merge's
+            // reads along d (one head, consecutive d) are both free of bank conflicts.
             float* mw = merge_s + warp * kHeads * D;
 #pragma unroll
             for (int mt = 0; mt < D / 16; ++mt) {
-                const int d0 = 16 * mt + g;
-                mw[(2 * t) * D + d0] = acc[mt][0];
-                mw[(2 * t + 1) * D + d0] = acc[mt][1];
-                mw[(2 * t) * D + d0 + 8] = acc[mt][2];
-                mw[(2 * t + 1) * D + d0 + 8] = acc[mt][3];
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int d = 16 * mt + g + 8 * hf, f = (d >> 2) & 7;
+                    const float a = acc[mt][2 * hf], c = acc[mt][2 * hf + 1];
+                    *reinterpret_cast<float2*>(mw + d * kHeads + ((2 * t) ^ (f & 6))) =
+                        (f & 1) ? make_float2(c, a) : make_float2(a, c);
+                }
             }
             if (g == 0) {
                 ml_s[(warp * kHeads + 2 * t) * 2 + 0] = m0;
@@ -577,86 +593,109 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         }
         __syncthreads();
         float* slot = p.partials + (int64_t)my_slot * kHeads * (D + 2);
-        for (int e = tid; e < kHeads * D; e += kThreads) {
-            const int hl = e / D, d = e - hl * D;
-            if (hl >= nh) continue;
+        if (tid < kHeads) {
+            // per head: the four warps' weights 2^(m_w - M) (in place of m_w) and the
+            // combined sum (in place of warp 0's l); a split piece also publishes (M, sum)
+            const int hl = tid;
             float M = kNegInf;
 #pragma unroll
             for (int w = 0; w < kWarps; ++w) M = fmaxf(M, ml_s[(w * kHeads + hl) * 2]);
             const float base = M == kNegInf ? 0.f : M;
-            float o = 0.f, l = 0.f;
+            float l = 0.f;
 #pragma unroll
             for (int w = 0; w < kWarps; ++w) {
                 const float f = fast_exp2(ml_s[(w * kHeads + hl) * 2] - base);
-                o += f * merge_s[(w * kHeads + hl) * D + d];
                 l += f * ml_s[(w * kHeads + hl) * 2 + 1];
+                ml_s[(w * kHeads + hl) * 2] = f;
             }
-            if (n_split == 1) {
-                store_from_float(p.out, ((int64_t)b * p.Hq + h0 + hl) * D + d, o / l, p.out_dtype);
-            } else {
-                slot[hl * D + d] = o;
-                if (d == 0) {
-                    slot[kHeads * D + hl] = base;
-                    slot[kHeads * D + kHeads + hl] = l;
-                }
+            ml_s[hl * 2 + 1] = l;
+            if (n_split > 1) {
+                slot[kHeads * D + hl] = base;
+                slot[kHeads * D + kHeads + hl] = l;
             }
         }
+        __syncthreads();
+        for (int e = tid; e < nh * D; e += kThreads) {
+            const int hl = e / D, d = e - hl * D;
+            const int sw = d * kHeads + (hl ^ ((d >> 2) & 7));
+            float o = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) o += ml_s[(w * kHeads + hl) * 2] * merge_s[w * kHeads * D + sw];
+            if (n_split == 1) store_from_float(p.out, ((int64_t)b * p.Hq + h0 + hl) * D + d, o / ml_s[hl * 2 + 1],
+                                               p.out_dtype);
+            else slot[hl * D + d] = o;
+        }
         if (n_split > 1) {
-            __threadfence();
+            // publish the slot (one fence after the barrier orders every thread's stores
+            // before the counter update), then count the unit's finished pieces
             __syncthreads();
             int* counter = p.counters + unit;
-            if (tid == 0) misc[8] = (atomicAdd(counter, 1) == n_split - 1);
+            if (tid == 0) {
+                __threadfence();
+                const int last = atomicAdd(counter, 1) == n_split - 1;
+                if (last) __threadfence();
+                misc[8] = last;
+            }
             __syncthreads();
             if (misc[8]) {
                 // Last piece of the unit: log-sum-exp combine of its n_split
                 // partial slots.  The piece of CTA c sits in slot 2c, or 2c+1
                 // when the unit starts inside c's range after its first piece.
-                // Each thread combines its own output elements; the loads of up to
-                // kMergeBatch slots are all issued before any is used (one L2 round
-                // trip per batch instead of three dependent ones).
-                __threadfence();
+                // A thread owns float4 groups of 4 consecutive d of one head; the loads of
+                // up to kBatch slots are all issued before any is used (one L2 round trip
+                // per batch).
                 auto slot_of = [&](int c) {
                     const int sub = (c == c0 && u_start != (long long)c0 * R) ? 1 : 0;
                     return p.partials + (int64_t)(2 * c + sub) * kHeads * (D + 2);
                 };
-                constexpr int kPer = kHeads * D / kThreads;  // output elements per thread
-                constexpr int kMergeBatch = kPer <= 4 ? 4 : (kPer <= 8 ? 2 : 1);
-                float o[kPer], lsum[kPer], mrun[kPer];
+                constexpr int kQ4 = kHeads * D / 4;                     // float4 groups of a slot's O
+                constexpr int kPer = (kQ4 + kThreads - 1) / kThreads;  // per thread: 1, 2, 2, 4
+                constexpr int kBatch = kPer == 1 ? 8 : (kPer == 2 ? 4 : 2);
+                float4 o[kPer];
+                float lsum[kPer], mrun[kPer];
 #pragma unroll
                 for (int j = 0; j < kPer; ++j) {
-                    o[j] = 0.f;
+                    o[j] = make_float4(0.f, 0.f, 0.f, 0.f);
                     lsum[j] = 0.f;
                     mrun[j] = kNegInf;
                 }
-                for (int cb = 0; cb < n_split; cb += kMergeBatch) {
-                    float mv[kMergeBatch][kPer], lv[kMergeBatch][kPer], ov[kMergeBatch][kPer];
+                for (int cb = 0; cb < n_split; cb += kBatch) {
+                    float4 ov[kBatch][kPer];
+                    float mv[kBatch][kPer], lv[kBatch][kPer];
 #pragma unroll
-                    for (int i = 0; i < kMergeBatch; ++i) {
+                    for (int i = 0; i < kBatch; ++i) {
                         if (cb + i >= n_split) break;
                         const float* sl = slot_of(c0 + cb + i);
 #pragma unroll
                         for (int j = 0; j < kPer; ++j) {
-                            const int e = tid + j * kThreads, hl = e / D;
+                            const int q4 = tid + j * kThreads, hl = min(q4, kQ4 - 1) * 4 / D;
+                            ov[i][j] = q4 < kQ4 ? __ldcg(reinterpret_cast<const float4*>(sl) + q4)
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
                             mv[i][j] = __ldcg(sl + kHeads * D + hl);
                             lv[i][j] = __ldcg(sl + kHeads * D + kHeads + hl);
-                            ov[i][j] = __ldcg(sl + e);
                         }
                     }
 #pragma unroll
                     for (int j = 0; j < kPer; ++j) {
                         float M = mrun[j];
 #pragma unroll
-                        for (int i = 0; i < kMergeBatch; ++i)
+                        for (int i = 0; i < kBatch; ++i)
                             if (cb + i < n_split) M = fmaxf(M, mv[i][j]);
                         const float base = M == kNegInf ? 0.f : M;
                         const float keep = fast_exp2(mrun[j] - base);  // 0 for the first batch
-                        o[j] *= keep;
+                        o[j].x *= keep;
+                        o[j].y *= keep;
+                        o[j].z *= keep;
+                        o[j].w *= keep;
                         lsum[j] *= keep;
 #pragma unroll
-                        for (int i = 0; i < kMergeBatch; ++i) {
+                        for (int i = 0; i < kBatch; ++i) {
                             if (cb + i >= n_split) break;
                             const float f = fast_exp2(mv[i][j] - base);
-                            o[j] += f * ov[i][j];
+                            o[j].x += f * ov[i][j].x;
+                            o[j].y += f * ov[i][j].y;
+                            o[j].z += f * ov[i][j].z;
+                            o[j].w += f * ov[i][j].w;
                             lsum[j] += f * lv[i][j];
                         }
                         mrun[j] = M;
@@ -664,11 +703,16 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
                 }
 #pragma unroll
                 for (int j = 0; j < kPer; ++j) {
-                    const int e = tid + j * kThreads;
-                    const int hl = e / D, d = e - hl * D;
-                    if (hl < nh)
-                        store_from_float(p.out, ((int64_t)b * p.Hq + h0 + hl) * D + d, o[j] / lsum[j],
-                                         p.out_dtype);
+                    const int q4 = tid + j * kThreads;
+                    if (q4 >= kQ4) break;
+                    const int hl = q4 * 4 / D, d = q4 * 4 - hl * D;
+                    if (hl < nh) {
+                        const int64_t oi = ((int64_t)b * p.Hq + h0 + hl) * D + d;
+                        store_from_float(p.out, oi + 0, o[j].x / lsum[j], p.out_dtype);
+                        store_from_float(p.out, oi + 1, o[j].y / lsum[j], p.out_dtype);
+                        store_from_float(p.out, oi + 2, o[j].z / lsum[j], p.out_dtype);
+                        store_from_float(p.out, oi + 3, o[j].w / lsum[j], p.out_dtype);
+                    }
                 }
                 if (tid == 0) *counter = 0;
             }
