@@ -26,11 +26,13 @@ B2A_API int b2a_test_inject_wait_timeout(b2a_context* ctx);
 /* The kernel family the context's last whole-sequence attention launch (b2a_mha,
  * b2a_prefill_causal, b2a_prefill_gemma) took, so that tests can assert the path:
  * B2A_TEST_KERNEL_TCGEN05 (tensor cores, TMEM, TMA), B2A_TEST_KERNEL_WARP_MMA
- * (mma.sync), B2A_TEST_KERNEL_GENERIC (fp32 / odd head dims); 0 before any launch
+ * (mma.sync), B2A_TEST_KERNEL_GENERIC (fp32 / odd head dims), B2A_TEST_KERNEL_F32_TILED
+ * (fp32 at head_dim 64 / 128); 0 before any launch
  * or for a null context. */
 #define B2A_TEST_KERNEL_TCGEN05 1
 #define B2A_TEST_KERNEL_WARP_MMA 2
 #define B2A_TEST_KERNEL_GENERIC 3
+#define B2A_TEST_KERNEL_F32_TILED 4
 B2A_API int b2a_test_last_attention_kernel(const b2a_context* ctx);
 
 #ifdef __cplusplus

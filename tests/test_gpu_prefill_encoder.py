@@ -33,6 +33,7 @@ def test_prefill_smollm2_config_fp32(ctx):
     """configs[0] exactly: B=1, S=256, 9/3 heads, D=64, NeoX RoPE theta 1e5, fp32 in/out."""
     got, want = _prefill_case(ctx, B=1, S=256, Hq=9, Hkv=3, D=64, dtype=oracle.F32, out_dtype=oracle.F32,
                               theta=1e5, seed=1)
+    assert ctx.last_attention_kernel() == "f32_tiled"
     err, _ = assert_close(got, want, atol=2e-3, what="smollm2 prefill")
     assert err < 1e-4  # fp32 end to end
 
@@ -327,11 +328,12 @@ def test_generic_kernel_key_split_back_to_back(ctx):
                                 rope_mode=b200attn.ROPE_NEOX, rope_theta=1e4, window=window)
         cases.append((o, want, f"fp32 prefill S={S} D={D} window={window}"))
     lens = [200, 17, 1]
-    shape = (3, 4, 200, 64)  # head-major encoder, fp32, key padding
+    shape = (3, 4, 200, 48)  # head-major encoder, fp32, key padding (head dim 48: the generic kernel)
     q, k, v = (normal(730 + j, shape, oracle.F32) for j in range(3))
-    want = oracle.encoder_minilm(q, k, v, lens, B=3, H=4, S=200, D=64, layout=0)
+    want = oracle.encoder_minilm(q, k, v, lens, B=3, H=4, S=200, D=48, layout=0)
     y = torch.full(shape, float("nan"), dtype=torch.float32, device="cuda")
-    b200attn.mha(ctx, to_dev(q, oracle.F32), to_dev(k, oracle.F32), to_dev(v, oracle.F32), y, 1.0 / 8.0,
+    b200attn.mha(ctx, to_dev(q, oracle.F32), to_dev(k, oracle.F32), to_dev(v, oracle.F32), y,
+                 float(np.float32(1.0 / math.sqrt(48))),
                  key_lengths=torch.from_numpy(np.asarray(lens, np.int32)).cuda(), layout=b200attn.HEAD_MAJOR)
     cases.append((y, want, "fp32 encoder, key lengths"))
     torch.cuda.synchronize()
@@ -347,16 +349,18 @@ def test_generic_kernel_runs_unsplit_without_room_for_the_split_workspace():
     import torch
     import b200attn
     lens = [200, 60]
-    shape = (2, 2, 200, 64)  # head-major fp32 encoder: needs no staging, would split (few query blocks)
+    shape = (2, 2, 200, 48)  # head-major fp32 encoder, head dim 48 (the generic kernel): would split
     q, k, v = (normal(760 + j, shape, oracle.F32) for j in range(3))
-    want = oracle.encoder_minilm(q, k, v, lens, B=2, H=2, S=200, D=64, layout=0)
+    want = oracle.encoder_minilm(q, k, v, lens, B=2, H=2, S=200, D=48, layout=0)
     with b200attn.Context(0) as small:
         small.set_workspace_limit(4096)
         y = torch.full(shape, float("nan"), dtype=torch.float32, device="cuda")
-        b200attn.mha(small, to_dev(q, oracle.F32), to_dev(k, oracle.F32), to_dev(v, oracle.F32), y, 1.0 / 8.0,
+        b200attn.mha(small, to_dev(q, oracle.F32), to_dev(k, oracle.F32), to_dev(v, oracle.F32), y,
+                     float(np.float32(1.0 / math.sqrt(48))),
                      key_lengths=torch.from_numpy(np.asarray(lens, np.int32)).cuda(), layout=b200attn.HEAD_MAJOR)
         torch.cuda.synchronize()
         small.check_device_status()
+        assert small.last_attention_kernel() == "generic"
         assert small.workspace_bytes() <= 4096
         err, _ = assert_close(to_np(y), want, what="unsplit fp32 encoder under a workspace limit")
         assert err < 1e-4
@@ -381,6 +385,51 @@ def test_fp32_prefill_rotates_in_kernel_from_the_cached_table(ctx):
         b200attn.prefill_causal(ctx, to_dev(q, oracle.F32), to_dev(k, oracle.F32), to_dev(v, oracle.F32), o, scale,
                                 rope_mode=b200attn.ROPE_NEOX, rope_theta=theta, pos0=pos0)
         torch.cuda.synchronize()
-        assert ctx.last_attention_kernel() == "generic"
+        assert ctx.last_attention_kernel() == ("f32_tiled" if D in (64, 128) else "generic")
         err, _ = assert_close(to_np(o), want, what=f"fused-rope fp32 prefill {i}")
         assert err < 1e-4
+
+
+# ------------------------------------------------------------------ fp32 tiled kernel
+@pytest.mark.parametrize("D,S,window,pos0,rope", [(64, 200, 0, 0, True), (128, 333, 0, 17, True),
+                                                   (64, 300, 100, 5, True), (128, 150, 40, 0, False),
+                                                   (64, 1, 0, 0, True), (64, 1040, 0, 0, True)])
+def test_fp32_tiled_causal_prefill(ctx, D, S, window, pos0, rope):
+    """fp32 causal prefill on the tiled fp32 kernel (16 query rows per CTA, key tiles alternating between two
+    warp halves): GQA, ragged last query block and key tile, a sliding window whose start moves inside a tile,
+    a position offset into the rotation table, no RoPE, one row, and a sequence whose 17 key tiles give the
+    halves unequal tile counts."""
+    got, want = _prefill_case(ctx, B=2, S=S, Hq=6, Hkv=2, D=D, dtype=oracle.F32, out_dtype=oracle.F32,
+                              theta=1e4, window=window, pos0=pos0, seed=900 + D + S, rope=rope)
+    assert ctx.last_attention_kernel() == "f32_tiled"
+    err, _ = assert_close(got, want, what=f"fp32 tiled prefill D={D} S={S} window={window}")
+    assert err < 1e-4  # fp32 end to end
+
+
+@pytest.mark.parametrize("layout,D,S", [(0, 64, 150), (1, 128, 77), (1, 64, 256)])
+def test_fp32_tiled_encoder_key_lengths(ctx, layout, D, S):
+    """Bidirectional fp32 encoder on the tiled kernel: key lengths of 0 (every key masked: the mean of V),
+    1, a ragged one and the full sequence, in both layouts."""
+    got, want = _encoder_case(ctx, B=4, H=3, S=S, D=D, dtype=oracle.F32, lens=[S, 0, 1, S // 2 + 3], layout=layout,
+                              seed=950 + D)
+    assert ctx.last_attention_kernel() == "f32_tiled"
+    err, _ = assert_close(got, want, what=f"fp32 tiled encoder D={D} S={S}")
+    assert err < 1e-4
+
+
+def test_fp32_tiled_additive_mask(ctx):
+    import torch
+    import b200attn
+    B, H, S, D = 3, 2, 130, 64
+    q, k, v = (normal(980 + i, (B, H, S, D), oracle.F32) for i in range(3))
+    mask = (normal(985, (B, S), oracle.F32) * 2.0).astype(np.float32)
+    mask[1, 7:] = -1e9
+    scale = float(np.float32(1.0 / math.sqrt(D)))
+    want = oracle.mha_additive(q, k, v, mask, B=B, H=H, S=S, D=D, scale=scale)
+    y = torch.full((B, H, S, D), float("nan"), device="cuda")
+    b200attn.mha(ctx, to_dev(q, oracle.F32), to_dev(k, oracle.F32), to_dev(v, oracle.F32), y, scale,
+                 mask=torch.from_numpy(mask).cuda())
+    torch.cuda.synchronize()
+    assert ctx.last_attention_kernel() == "f32_tiled"
+    err, _ = assert_close(to_np(y), want, what="fp32 tiled additive mask")
+    assert err < 1e-4

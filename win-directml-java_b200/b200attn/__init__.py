@@ -216,8 +216,9 @@ class Context:
 
     def last_attention_kernel(self) -> str:
         """Test hook (include/b200attn_testing.h): the kernel family of the last whole-sequence
-        attention launch: "tcgen05", "warp_mma", "generic" or "" before any."""
-        return {1: "tcgen05", 2: "warp_mma", 3: "generic"}.get(lib().b2a_test_last_attention_kernel(self._h), "")
+        attention launch: "tcgen05", "warp_mma", "generic", "f32_tiled" or "" before any."""
+        return {1: "tcgen05", 2: "warp_mma", 3: "generic", 4: "f32_tiled"}.get(
+            lib().b2a_test_last_attention_kernel(self._h), "")
 
     def inject_wait_timeout(self):
         """Test hook (include/b200attn_testing.h): the next tcgen05 attention launch of this

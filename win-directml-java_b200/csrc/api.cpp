@@ -195,7 +195,8 @@ int check_head_dim(b2a_context* ctx, int D) {
 }
 
 // Whole-sequence attention: the tcgen05 kernel where its shape rules hold,
-// else the warp-MMA kernel (16-bit, head_dim 32..128), else the generic one.
+// else the warp-MMA kernel (16-bit, head_dim 32..128), else the tiled fp32 kernel
+// (fp32, head_dim 64 / 128), else the generic one.
 cudaError_t launch_attention(b2a_context* ctx, const AttnParams& p, cudaStream_t s) {
     if (attn_tcgen05_supported(p)) {
         const bool stall = ctx->inject_wait_timeout;
@@ -206,6 +207,10 @@ cudaError_t launch_attention(b2a_context* ctx, const AttnParams& p, cudaStream_t
     if (attn_tc_supported(p)) {
         ctx->last_attention_kernel = B2A_TEST_KERNEL_WARP_MMA;
         return launch_attn_tc(p, s);
+    }
+    if (attn_f32_supported(p)) {
+        ctx->last_attention_kernel = B2A_TEST_KERNEL_F32_TILED;
+        return launch_attn_f32(p, s);
     }
     ctx->last_attention_kernel = B2A_TEST_KERNEL_GENERIC;
     // generic kernel: launches too small to fill the GPU split each query block's keys
@@ -562,7 +567,7 @@ B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype, co
     const size_t nq = (size_t)B * S * Hq * D, nk = (size_t)B * S * Hkv * D;
     auto r256 = [](size_t x) { return (x + 255) / 256 * 256; };
 
-    // fp32 inputs (the generic kernel) with the NeoX rotation and no rotated-key output: the
+    // fp32 inputs (the fp32 kernels) with the NeoX rotation and no rotated-key output: the
     // kernel rotates q and k itself from the context's cached table -- one launch, no pre-pass
     if (in_dtype == B2A_FLOAT32 && rope_mode == B2A_ROPE_NEOX && k_rot_out == nullptr) {
         const float2* tab = nullptr;

@@ -95,7 +95,7 @@ struct AttnParams {
     float scale;
     // NeoX RoPE applied inside the kernel to q and k at position rope_pos0 + s: float (cos, sin)
     // [position][D/2] covering positions [0, rope_pos0 + S), or NULL (q and k are used as given).
-    // Only the generic kernel (attn_simt.cu) takes it.
+    // Only the fp32 kernels (attn_f32.cu, attn_simt.cu) take it.
     const float2* rope_table;
     int rope_pos0;
     // tcgen05 kernel only: 7 = q, k and v are bf16 (in_dtype) and the kernel converts each staged
@@ -115,6 +115,9 @@ struct SimtSplit {
 // Chunks per query block for this launch (1: no split) and the workspace it needs.
 int attn_simt_split_plan(const AttnParams& p, int sm_count, size_t* part_bytes, size_t* counter_ints);
 cudaError_t launch_attn_simt(const AttnParams& p, cudaStream_t stream, const SimtSplit* split = nullptr);
+// fp32 inputs at head_dim 64 / 128 (attn_f32.cu): 16 query rows per CTA, no key split.
+bool attn_f32_supported(const AttnParams& p);
+cudaError_t launch_attn_f32(const AttnParams& p, cudaStream_t stream);
 // The context's device status buffer: words [0, kStatusWords) are the error flags
 // b2a_check_device_status reports and clears; words kStatusSchedWord and the next one are
 // the persistent prefill kernel's work-item counters, and word kStatusAbortWord its
