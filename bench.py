@@ -189,7 +189,7 @@ def decode_config(name: str, B: int, lens, max_seq: int) -> dict:
 class DecodeWorkload:
     """configs[4] (c5) or configs[2] (c3): one decode token for every sequence."""
 
-    def __init__(self, name: str, seed: int, batch: int = 0, world: int = 1, rank: int = 0):
+    def __init__(self, name: str, seed: int, batch: int = 0, world: int = 1, rank: int = 0, n_layers: int = 1):
         import torch
         import b200attn
         self.torch, self.b2a, self.name = torch, b200attn, name
@@ -199,7 +199,8 @@ class DecodeWorkload:
             self.layout, self.rope, self.norm = b200attn.KV_POS_MAJOR, b200attn.ROPE_GEMMA, True
         else:
             self.B, self.Hq, self.Hkv, self.D, self.lo, self.hi = 64, 14, 2, 64, 512, 8192
-            self.layers = [dict(window=0, theta=1e6)]
+            # n_layers > 1: a model step, every layer with its own cache (the same sequences)
+            self.layers = [dict(window=0, theta=1e6) for _ in range(n_layers)]
             self.layout, self.rope, self.norm = b200attn.KV_HEAD_MAJOR, b200attn.ROPE_NEOX, False
         if batch > 0:  # smaller batch for profiler captures only
             self.B = batch
@@ -350,7 +351,7 @@ class DecodeWorkload:
 class PrefillWorkload:
     """c1 / c4: causal prefill with fused RoPE; c2: masked encoder."""
 
-    def __init__(self, name: str, seed: int, batch: int = 0):
+    def __init__(self, name: str, seed: int, batch: int = 0, n_layers: int = 1):
         import torch
         import b200attn
         from b200attn import synthetic
@@ -369,30 +370,43 @@ class PrefillWorkload:
         mk = lambda h: torch.randn(self.B, self.S, h, self.D, generator=g, device="cuda").to(self.dt)
         self.q, self.k, self.v = mk(self.Hq), mk(self.Hkv), mk(self.Hkv)
         self.o = torch.empty_like(self.q)
+        # n_layers > 1: a model step, every layer with its own q, k, v, o (the same sequences)
+        self.layer_tensors = [(self.q, self.k, self.v, self.o)]
+        for _ in range(n_layers - 1):
+            q, k, v = mk(self.Hq), mk(self.Hkv), mk(self.Hkv)
+            self.layer_tensors.append((q, k, v, torch.empty_like(q)))
         self.scale = 1.0 / math.sqrt(self.D)
 
     def tokens_per_step(self):
         return self.B * self.S
 
     def kernel_launches_per_step(self):
-        return 1 if self.name == "c2" else 3  # rope table, one pre-pass (rope q, k; convert), attention
+        # c2: attention; c1 (fp32): attention rotating q and k itself from the context's cached table;
+        # c4 (bf16): rope table, one pre-pass (rope q, k; convert q, k, v), attention
+        per_layer = 3 if self.name == "c4" else 1
+        return per_layer * len(self.layer_tensors)
 
     def flops(self):
+        """Summed over the step's layers."""
         if self.name == "c2":
-            return 4 * self.Hq * self.D * self.S * int(self.lens.astype(np.int64).sum())
-        return 4 * self.B * self.Hq * self.D * self.S * (self.S + 1) // 2
+            per = 4 * self.Hq * self.D * self.S * int(self.lens.astype(np.int64).sum())
+        else:
+            per = 4 * self.B * self.Hq * self.D * self.S * (self.S + 1) // 2
+        return per * len(self.layer_tensors)
 
     def algorithmic_bytes(self):
+        """Summed over the step's layers."""
         e = self.q.element_size()
-        return e * self.B * self.S * self.D * (2 * self.Hq + 2 * self.Hkv)
+        return e * self.B * self.S * self.D * (2 * self.Hq + 2 * self.Hkv) * len(self.layer_tensors)
 
     def step(self, ctx, stream=None):
-        if self.name == "c2":
-            self.b2a.mha(ctx, self.q, self.k, self.v, self.o, self.scale, key_lengths=self.lens_d,
-                         layout=self.b2a.SEQ_MAJOR, stream=stream)
-        else:
-            self.b2a.prefill_causal(ctx, self.q, self.k, self.v, self.o, self.scale, rope_mode=self.b2a.ROPE_NEOX,
-                                    rope_theta=self.theta, stream=stream)
+        for q, k, v, o in self.layer_tensors:
+            if self.name == "c2":
+                self.b2a.mha(ctx, q, k, v, o, self.scale, key_lengths=self.lens_d, layout=self.b2a.SEQ_MAJOR,
+                             stream=stream)
+            else:
+                self.b2a.prefill_causal(ctx, q, k, v, o, self.scale, rope_mode=self.b2a.ROPE_NEOX,
+                                        rope_theta=self.theta, stream=stream)
 
 
 class BlockWorkload:
@@ -518,10 +532,43 @@ def run_suite(ctx, hbm, tflops, src):
         entry["tensor_frac"] = round(tfs / tflops, 4)
         entry["bound"] = "tensor" if name == "c4" else "hbm"
         entry["peak_source"] = src
-        out[name] = entry
         del w
         torch.cuda.empty_cache()
+        if name in MODEL_LAYERS:
+            entry["model_step"] = model_step_entry(ctx, torch, name, hbm, time_steps_fn=time_steps, flush=flush)
+        out[name] = entry
     return out
+
+
+# Layers of the model each latency-bound suite config is shaped on: SmolLM2-135M (30), MiniLM-L6 (6),
+# Qwen2.5-0.5B (24).  Their attention launches run back to back in a real forward or decode step.
+MODEL_LAYERS = {"c1": 30, "c2": 6, "c3": 24}
+
+
+def model_step_entry(ctx, torch, name, hbm, time_steps_fn, flush):
+    """The config's attention over every layer of its model in one step: each layer has its own
+    tensors (caches), the layers' launches run back to back in one CUDA graph, L2 is flushed before
+    each step.  Reports the time per layer, where a single launch's fixed cost (the launch and the
+    first loads of every CTA) overlaps the previous layer as it does in a model."""
+    L = MODEL_LAYERS[name]
+    w = DecodeWorkload(name, 3, n_layers=L) if name == "c3" else \
+        PrefillWorkload(name, {"c1": 1, "c2": 2}[name], n_layers=L)
+    for _ in range(2):
+        w.step(ctx)
+    torch.cuda.synchronize()
+    g = capture_graph(torch, lambda: w.step(ctx))
+    ms = statistics.mean(time_steps_fn(torch, (lambda: g.replay()) if g is not None else (lambda: w.step(ctx)),
+                                       5, flush))
+    del g
+    per = ms / L
+    gbs = w.algorithmic_bytes() / L / (per / 1e3) / 1e9
+    entry = {"layers": L, "ms_per_step": round(ms, 4), "ms_per_layer": round(per, 4),
+             "hbm_gbs_per_layer": round(gbs, 1), "hbm_frac_per_layer": round(gbs / hbm, 4),
+             "tokens_per_s": round(w.tokens_per_step() / (ms / 1e3), 1),
+             "l2": "flushed before each step; every layer's tensors distinct"}
+    del w
+    torch.cuda.empty_cache()
+    return entry
 
 
 # ------------------------------------------------------------------ CPU reference arm
