@@ -588,6 +588,9 @@ B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype, co
     const size_t ce = dtype_size(cdt);
     const bool rope = rope_mode != B2A_ROPE_NONE;
     const bool conv = cdt != in_dtype;
+    // the vectorised pre-pass reads NeoX (cos, sin) rows from the context's cached float table;
+    // Gemma's double table (and the row-wise fallback's) is built per call into the workspace
+    const bool cached_table = rope_mode == B2A_ROPE_NEOX;
     const size_t table_bytes = rope ? r256((size_t)S * (D / 2) * 16) : 0;
     const size_t q_bytes = (rope || conv) ? r256(nq * ce) : 0;
     const bool k_in_out = rope && !conv && k_rot_out != nullptr;  // rotated keys land in k_rot_out directly
@@ -606,15 +609,24 @@ B2A_API int b2a_prefill_causal(b2a_context* ctx, int in_dtype, int out_dtype, co
     const void* prep_ptrs[] = {q, k, v, q_c, k_c, v_c, k_rot_out};
     const bool vec_prep = (rope || conv) && prep_vectorizable(D, (int64_t)std::max(nq, nk), prep_ptrs, 7);
     if (vec_prep) {
-        // one table build + one launch: q and k rotated / converted, v converted
+        // one launch: q and k rotated / converted, v converted (NeoX: from the cached table,
+        // else after a table build)
         double inv[kMaxHeadDim / 2] = {};
         if (rope) inv_freq_table(rope_theta, D, inv);
+        double2* prep_table = table;
+        if (rope && cached_table) {
+            const float2* tab = nullptr;
+            if ((int64_t)pos0 + S > INT32_MAX) return fail(ctx, B2A_EINVAL, "pos0 + S exceeds the position range");
+            if ((rc = neox_table(ctx, rope_theta, D, pos0 + S, s, &tab))) return rc;
+            prep_table = reinterpret_cast<double2*>(const_cast<float2*>(tab + (size_t)pos0 * (D / 2)));
+        }
         PrepJob jobs[3];
         int nj = 0;
         jobs[nj++] = PrepJob{q, q_c, nullptr, Hq, rope ? 1 : 0};
         jobs[nj++] = PrepJob{k, k_c, (rope && k_rot_out && !k_in_out) ? k_rot_out : nullptr, Hkv, rope ? 1 : 0};
         if (conv) jobs[nj++] = PrepJob{v, v_c, nullptr, Hkv, 0};
-        e = launch_prep(jobs, nj, B, S, D, in_dtype, cdt, pos0, rope_mode, inv, table, ctx->status, s);
+        e = launch_prep(jobs, nj, B, S, D, in_dtype, cdt, pos0, rope_mode, inv, prep_table, ctx->status, s,
+                        rope && cached_table);
         if (e == cudaSuccess && !rope && k_rot_out)
             e = cudaMemcpyAsync(k_rot_out, k, nk * dtype_size(in_dtype), cudaMemcpyDeviceToDevice, s);
     } else if (rope) {
@@ -682,6 +694,9 @@ B2A_API int b2a_prefill_gemma(b2a_context* ctx, int in_dtype, int out_dtype, con
     auto r256 = [](size_t x) { return (x + 255) / 256 * 256; };
     const bool rope = rope_mode != B2A_ROPE_NONE;
     const bool conv = cdt != in_dtype;
+    // the vectorised pre-pass reads NeoX (cos, sin) rows from the context's cached float table;
+    // Gemma's double table (and the row-wise fallback's) is built per call into the workspace
+    const bool cached_table = rope_mode == B2A_ROPE_NEOX;
     const size_t table_bytes = rope ? r256((size_t)S * (D / 2) * 16) : 0;
     const size_t q_bytes = r256(nq * ce), k_bytes = r256(nk * ce), v_bytes = conv ? r256(nk * ce) : 0;
     rc = ensure_buffer(ctx, &ctx->pf_ws, &ctx->pf_ws_bytes, table_bytes + q_bytes + k_bytes + v_bytes, "prefill");

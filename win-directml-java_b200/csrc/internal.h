@@ -163,8 +163,11 @@ struct PrepJob {
 };
 // elems: the largest tensor's element count.
 bool prep_vectorizable(int D, int64_t elems, const void* const* ptrs, int n);
+// table_ready: `table` already holds the (cos, sin) rows of positions pos0 .. pos0 + S - 1 (the
+// context's cached NeoX table); otherwise the rows are built into it first.
 cudaError_t launch_prep(const PrepJob* jobs, int n_jobs, int B, int S, int D, int in_dtype, int out_dtype, int pos0,
-                        int rope_mode, const double* inv_freq, double2* table, int* status, cudaStream_t stream);
+                        int rope_mode, const double* inv_freq, double2* table, int* status, cudaStream_t stream,
+                        bool table_ready = false);
 
 // QK-norm + RoPE pre-pass (one warp per [b][s][h] row of a dense tensor): zero-centred
 // RMSNorm with (1 + w) when norm_w is set, rotation at pos0 + s (rope_mode 1 NeoX,

@@ -395,11 +395,12 @@ bool prep_vectorizable(int D, int64_t elems, const void* const* ptrs, int n) {
 }
 
 cudaError_t launch_prep(const PrepJob* jobs, int n_jobs, int B, int S, int D, int in_dtype, int out_dtype, int pos0,
-                        int rope_mode, const double* inv_freq, double2* table, int* status, cudaStream_t stream) {
+                        int rope_mode, const double* inv_freq, double2* table, int* status, cudaStream_t stream,
+                        bool table_ready) {
     const int half = D / 2;
     bool any_rotate = false;
     for (int i = 0; i < n_jobs; ++i) any_rotate |= jobs[i].rotate != 0;
-    if (any_rotate) {
+    if (any_rotate && !table_ready) {
         FreqTable f{};
         for (int i = 0; i < half; ++i) f.inv_freq[i] = inv_freq[i];
         const int64_t n = (int64_t)S * half;
