@@ -382,8 +382,8 @@ class PrefillWorkload:
 
     def kernel_launches_per_step(self):
         # c2: attention; c1 (fp32): attention rotating q and k itself from the context's cached table;
-        # c4 (bf16): rope table, one pre-pass (rope q, k; convert q, k, v), attention
-        per_layer = 3 if self.name == "c4" else 1
+        # c4 (bf16): one pre-pass (rope q, k from the cached table; convert q, k, v), attention
+        per_layer = 2 if self.name == "c4" else 1
         return per_layer * len(self.layer_tensors)
 
     def flops(self):
