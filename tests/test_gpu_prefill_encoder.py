@@ -270,6 +270,7 @@ def test_encoder_bf16_beyond_the_fp16_range_is_flagged(ctx):
     (oracle.BF16, 0, 1e6, 96, 256),     # global layer
     (oracle.F16, 40, 1e4, 130, 128),    # a tensor-core head dim, ragged last tile
     (oracle.F32, 0, 1e6, 48, 256),      # fp32 end to end
+    (oracle.F32, 40, 1e4, 150, 128),    # fp32 on the tiled fp32 kernel, window inside a key tile
     (oracle.BF16, 512, 1e4, 700, 256),  # local layer over several 128-row tiles (tensor cores, one tile per item)
     (oracle.F16, 0, 1e6, 600, 256),     # global layer, fp16
 ])
@@ -404,6 +405,16 @@ def test_fp32_tiled_causal_prefill(ctx, D, S, window, pos0, rope):
     assert ctx.last_attention_kernel() == "f32_tiled"
     err, _ = assert_close(got, want, what=f"fp32 tiled prefill D={D} S={S} window={window}")
     assert err < 1e-4  # fp32 end to end
+
+
+@pytest.mark.parametrize("out_dtype", [oracle.BF16, oracle.F16])
+def test_fp32_tiled_prefill_16bit_output(ctx, out_dtype):
+    """fp32 inputs with a 16-bit output: the tiled fp32 kernel rounds its fp32 result once on store."""
+    got, want = _prefill_case(ctx, B=1, S=130, Hq=4, Hkv=2, D=64, dtype=oracle.F32, out_dtype=out_dtype,
+                              theta=1e4, seed=970)
+    assert ctx.last_attention_kernel() == "f32_tiled"
+    ulp = 2.0 ** -8 if out_dtype == oracle.BF16 else 2.0 ** -11
+    assert_close(got, want, atol=2e-3 + ulp * np.abs(want).max(), what=f"fp32 in, {TORCH[out_dtype]} out")
 
 
 @pytest.mark.parametrize("layout,D,S", [(0, 64, 150), (1, 128, 77), (1, 64, 256)])
