@@ -704,6 +704,9 @@ def main():
         if world > 1:
             dist.barrier()
     ctx = b200attn.Context(local)
+    # decode layers start while the kernel ahead of them finishes (b2a_set_decode_early_start):
+    # nothing launched here writes ctx_lens or the cache rows a decode reads right before it
+    ctx.set_decode_early_start(True)
     hbm, tflops, src = peaks()
 
     if args.workload == "c3blk":
@@ -828,7 +831,8 @@ def main():
             "dtype": "f16" if isinstance(w, (DecodeWorkload, BlockWorkload)) else str(w.dt).split(".")[-1],
             "data": "synthetic (seeded N(0,1); no dataset or checkpoint)",
             "config": dict(w.config() if isinstance(w, DecodeWorkload) else {"workload": WORKLOADS[args.workload]},
-                           parallelism=f"shard{world} (sequences per rank)", launch=launch_mode),
+                           parallelism=f"shard{world} (sequences per rank)", launch=launch_mode,
+                           decode_early_start=True),
             "roofline": roof,
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},

@@ -122,6 +122,16 @@ B2A_API const char* b2a_build_info(void);
  * attention kernel: without room for it the launch runs unsplit. */
 B2A_API int b2a_set_workspace_limit(b2a_context* ctx, size_t bytes);
 
+/* Early start for b2a_decode on the tensor-core path (enable != 0; off by default).
+ * Each decode launch is then made with programmatic stream serialisation: it plans its
+ * work from ctx_lens and requests its first KV-cache tiles while the kernel before it on
+ * the stream finishes, and waits for that kernel to complete before it reads q, the new
+ * k/v rows, biases or norm weights and before any write.  Contract: the kernel launched
+ * immediately before a decode on the same stream must not write ctx_lens or the cache
+ * rows below ctx_lens[b] (rows the decode reads) -- true of back-to-back decode layers and
+ * of projections that produce q / k / v.  Returns B2A_OK, or B2A_EINVAL for a null context. */
+B2A_API int b2a_set_decode_early_start(b2a_context* ctx, int enable);
+
 /* Bytes of device workspace the context currently holds. */
 B2A_API int b2a_workspace_bytes(const b2a_context* ctx, size_t* bytes);
 

@@ -6,6 +6,8 @@ compares the output with ``oracle.decode`` (max abs <= 2e-3, cosine >=
 0.9999) and the appended cache rows with the oracle's (one ulp of the cache
 type); every other cache row must be untouched (bit-exact).
 """
+import math
+
 import numpy as np
 import pytest
 
@@ -246,3 +248,81 @@ def test_decode_qwen_config_longest_contexts(ctx):
     lens = np.array([8192, 8191, 7000, 512, 4096, 8000], np.int32)
     _long_context_case(ctx, lens=lens, Hq=14, Hkv=2, D=64, max_seq=8193, layout=oracle.KV_HEAD_MAJOR,
                        rope_mode="neox", theta=1e6, window=0, qk_norm=False, seed=5100)
+
+
+def test_decode_early_start_layers_back_to_back(ctx):
+    """b2a_set_decode_early_start: a chain of decode layers (each with its own caches, as in a model
+    step; Qwen-shaped head-major and Gemma-shaped position-major with QK-norm) launched directly and
+    replayed from a CUDA graph gives the same bits as the same chain without early start, and the
+    first layer equals the oracle."""
+    import torch
+    import b200attn
+    L, B, S = 4, 24, 1200
+    lens = torch.from_numpy(np.asarray([(37 * i * i + 11) % (S - 1) for i in range(B)], np.int32)).cuda()
+    cases = []
+    for name, Hq, Hkv, D, layout, rope, norm in (("qwen", 14, 2, 64, b200attn.KV_HEAD_MAJOR, b200attn.ROPE_NEOX, False),
+                                                 ("gemma", 4, 1, 256, b200attn.KV_POS_MAJOR, b200attn.ROPE_GEMMA, True)):
+        shape = (B, Hkv, S, D) if layout == b200attn.KV_HEAD_MAJOR else (B, S, Hkv, D)
+        layers = []
+        for l in range(L):
+            seed = 1500 + 10 * l + (0 if name == "qwen" else 500)
+            q, kn, vn = (to_dev(normal(seed + i, s, oracle.F16), oracle.F16)
+                         for i, s in enumerate([(B, Hq, D), (B, Hkv, D), (B, Hkv, D)]))
+            kc, vc = to_dev(normal(seed + 3, shape, oracle.F16), oracle.F16), to_dev(normal(seed + 4, shape, oracle.F16), oracle.F16)
+            layers.append(dict(q=q, kn=kn, vn=vn, kc=kc, vc=vc, out=torch.empty((B, Hq, D), device="cuda")))
+        qw = torch.from_numpy((0.5 * normal(1590, (D,), oracle.F32)).astype(np.float32)).cuda() if norm else None
+        kw = torch.from_numpy((0.5 * normal(1591, (D,), oracle.F32)).astype(np.float32)).cuda() if norm else None
+        cases.append((name, Hq, Hkv, D, layout, rope, layers, qw, kw))
+
+    def chain(case):
+        name, Hq, Hkv, D, layout, rope, layers, qw, kw = case
+        for l, t in enumerate(layers):
+            b200attn.decode(ctx, t["q"], t["kn"], t["vn"], t["kc"], t["vc"], lens, t["out"], 1.0 / math.sqrt(D),
+                            kv_layout=layout, rope_mode=rope, rope_theta=1e4 if l % 2 else 1e6,
+                            window=512 if (name == "gemma" and l % 2) else 0, q_norm_w=qw, k_norm_w=kw,
+                            norm_eps=1e-6)
+
+    for case in cases:
+        layers = case[6]
+        ctx.set_decode_early_start(False)
+        chain(case)
+        torch.cuda.synchronize()
+        ctx.check_device_status()
+        ref = [t["out"].clone() for t in layers]
+        try:
+            ctx.set_decode_early_start(True)
+            for t in layers:
+                t["out"].fill_(float("nan"))
+            chain(case)  # direct launches
+            torch.cuda.synchronize()
+            ctx.check_device_status()
+            for l, t in enumerate(layers):
+                assert torch.equal(t["out"], ref[l]), f"{case[0]} layer {l}: early start changed the output"
+            for t in layers:
+                t["out"].fill_(float("nan"))
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    chain(case)
+            torch.cuda.current_stream().wait_stream(s)
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize()
+            ctx.check_device_status()
+            for l, t in enumerate(layers):
+                assert torch.equal(t["out"], ref[l]), f"{case[0]} layer {l}: graph replay with early start differs"
+            del g
+        finally:
+            ctx.set_decode_early_start(False)
+    # the first Qwen layer against the oracle (the chain's caches have the new rows appended; the
+    # oracle's append writes the same rows, so it starts from the appended caches as well)
+    name, Hq, Hkv, D, layout, rope, layers, qw, kw = cases[0]
+    t = layers[0]
+    want, _, _ = oracle.decode(to_np(t["q"]), to_np(t["kn"]), to_np(t["vn"]), to_np(t["kc"]), to_np(t["vc"]),
+                               lens.cpu().numpy(), B=B, Hq=Hq, Hkv=Hkv, D=D, max_seq=S,
+                               scale=float(np.float32(1.0 / math.sqrt(D))), rope_theta=1e6,
+                               rope_mode=oracle.ROPE_DECODERONLY, cache_layout=oracle.KV_HEAD_MAJOR,
+                               cache_dtype=oracle.F16)
+    assert_close(to_np(t["out"]), want, what="early-start chain, layer 0 against the oracle")

@@ -90,6 +90,7 @@ def lib() -> ctypes.CDLL:
         L.b2a_abi_version.restype = _i
         L.b2a_build_info.restype = ctypes.c_char_p
         L.b2a_set_workspace_limit.argtypes = [_vp, ctypes.c_size_t]
+        L.b2a_set_decode_early_start.argtypes = [_vp, _i]
         L.b2a_workspace_bytes.argtypes = [_vp, ctypes.POINTER(ctypes.c_size_t)]
         L.b2a_reserve_decode.argtypes = [_vp, _i, _i, _i, _i]
         L.b2a_check_device_status.argtypes = [_vp, _vp]
@@ -120,7 +121,8 @@ def lib() -> ctypes.CDLL:
         L.b2a_sharded_decode.argtypes = [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _f, _i,
                                          _d, _i, _vp, _vp, _f, _vp, _vp, _vp]
         L.b2a_sharded_mha.argtypes = [_vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _i, _vp]
-        for name in ("b2a_create", "b2a_destroy", "b2a_last_error", "b2a_set_workspace_limit", "b2a_workspace_bytes",
+        for name in ("b2a_create", "b2a_destroy", "b2a_last_error", "b2a_set_workspace_limit",
+                     "b2a_set_decode_early_start", "b2a_workspace_bytes",
                      "b2a_reserve_decode", "b2a_check_device_status", "b2a_mha", "b2a_prefill_causal", "b2a_decode",
                      "b2a_qwen_rope_and_append", "b2a_qwen_gqa_attention_decode", "b2a_qwen_decode_step", "b2a_prefill_gemma",
                      "b2a_gemma_fused_attention_context", "b2a_partition_units", "b2a_test_inject_wait_timeout",
@@ -202,6 +204,12 @@ class Context:
 
     def set_workspace_limit(self, nbytes: int):
         self.check(lib().b2a_set_workspace_limit(self._h, nbytes))
+
+    def set_decode_early_start(self, enable: bool):
+        """b2a_set_decode_early_start: tensor-core decodes overlap their plan and first cache
+        tiles with the kernel ahead of them on the stream (which must not write ctx_lens or the
+        cache rows the decode reads)."""
+        self.check(lib().b2a_set_decode_early_start(self._h, 1 if enable else 0))
 
     def workspace_bytes(self) -> int:
         n = ctypes.c_size_t()

@@ -57,6 +57,8 @@ struct b2a_context {
     // test hook (b2a_test_inject_wait_timeout): the next tcgen05 attention launch
     // leaves one K/V copy unissued
     bool inject_wait_timeout = false;
+    // b2a_set_decode_early_start: tensor-core decodes launched with programmatic serialisation
+    bool decode_early_start = false;
     // test hook (b2a_test_last_attention_kernel): the kernel the last whole-sequence
     // attention launch took
     int last_attention_kernel = 0;
@@ -250,6 +252,7 @@ int run_decode(b2a_context* ctx, DecodeParams& p, cudaStream_t stream, bool allo
         p.partials = reinterpret_cast<float*>(static_cast<char*>(ctx->dec_ws) + counter_bytes);
         p.target_items = target;
         p.item_capacity = cap;
+        p.early_start = ctx->decode_early_start ? 1 : 0;
         const int B = p.B;
         // one launch covers at most kDecodeMaxBatchPerLaunch sequences and a key
         // stream (visible keys plus per-unit overhead keys) below 2^31 (the kernel's int32 prefix)
@@ -371,6 +374,12 @@ B2A_API int b2a_last_error(const b2a_context* ctx, char* buf, size_t n) {
 B2A_API int b2a_set_workspace_limit(b2a_context* ctx, size_t bytes) {
     if (!ctx) return B2A_EINVAL;
     ctx->ws_limit = bytes;
+    return B2A_OK;
+}
+
+B2A_API int b2a_set_decode_early_start(b2a_context* ctx, int enable) {
+    if (!ctx) return B2A_EINVAL;
+    ctx->decode_early_start = enable != 0;
     return B2A_OK;
 }
 

@@ -218,6 +218,9 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
     float* vec = vec_all + warp * D;
+    // a decode launched after this one with early start may be scheduled from now on; it
+    // still waits for this grid's completion before it reads its inputs or writes
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     // ---------------------------------------------------------------- plan
     // Stream-K split: the visible keys of all units (sequence, kv head, head
@@ -298,6 +301,7 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
     const long long range_hi =
         aligned ? (blockIdx.x + 1) * n_units / n_cta * unit_len : min(total, range_lo + R);
 
+    bool dep_done = false;  // early start: the kernel before this one has completed
     // Where shared memory holds no copy of the lengths (head dim 256), the next sequence's
     // length is requested one piece ahead: a global read made when the piece needs it
     // waits behind the other CTAs' streams for about a microsecond.
@@ -347,6 +351,10 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         const int nh = min(kHeads, p.G - hg * kHeads);
 
         if (!ok) {
+            if (p.early_start && !dep_done) {  // no write before the kernel ahead has completed
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+                dep_done = true;
+            }
             for (int e = tid; e < nh * D; e += kThreads)
                 store_from_float(p.out, ((int64_t)b * p.Hq + h0 + e / D) * D + e % D, __int_as_float(0x7fc00000),
                                  p.out_dtype);
@@ -381,6 +389,20 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
         const bool rope = p.append && p.rope_mode != 0;
         double inv_f = 0.0;
         if (rope && tid < D / 2) inv_f = p.inv_freq[tid];  // a kernel-parameter array: plain load
+        // Early start (programmatic dependent launch): the first piece requests its cache tiles
+        // (rows below L, which the kernel before it on the stream does not write), then waits
+        // for that kernel to complete before reading anything it may have produced -- q, the
+        // new k/v rows, biases, norm weights -- and before any write.
+        const bool tiles_first = p.early_start && !dep_done;
+        if (tiles_first) {
+#pragma unroll
+            for (int s = 0; s < kStages - 1; ++s) {
+                if (s < n_tiles) load_tile(s, s);
+                cp_async_commit();
+            }
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            dep_done = true;
+        }
         constexpr int kHeadsPerWarp = kHeads / kWarps;
         static_assert(kHeads % kWarps == 0 && D / 2 <= kThreads, "prologue work split");
         HeadLoad<D> qload[kHeadsPerWarp];
@@ -406,10 +428,12 @@ __global__ void __launch_bounds__(kThreads) decode_tc_kernel(const __grid_consta
                          p.q_dtype, warp == 0 ? (p.k_bias ? p.k_bias + kvh * D : nullptr)
                                               : (p.v_bias ? p.v_bias + kvh * D : nullptr),
                          lane);
+        if (!tiles_first) {
 #pragma unroll
-        for (int s = 0; s < kStages - 1; ++s) {
-            if (s < n_tiles) load_tile(s, s);
-            cp_async_commit();
+            for (int s = 0; s < kStages - 1; ++s) {
+                if (s < n_tiles) load_tile(s, s);
+                cp_async_commit();
+            }
         }
 
         // ------------------------------------------------ prologue (q, new k/v)
@@ -789,16 +813,28 @@ cudaError_t launch_decode_tc(const DecodeParams& p, int device, cudaStream_t str
     cudaError_t err = cudaErrorInvalidValue;
     dispatch_dim(p.D, [&](auto dc) {
         constexpr int kD = decltype(dc)::value;
-        if (p.cache_dtype == kBF16) {
-            const LaunchInfo li = launch_info<kD, __nv_bfloat16>(device);
-            if (li.grid <= 0) { err = cudaErrorInvalidConfiguration; return; }
-            decode_tc_kernel<kD, __nv_bfloat16><<<li.grid, kThreads, li.smem, stream>>>(p);
-        } else {
-            const LaunchInfo li = launch_info<kD, __half>(device);
-            if (li.grid <= 0) { err = cudaErrorInvalidConfiguration; return; }
-            decode_tc_kernel<kD, __half><<<li.grid, kThreads, li.smem, stream>>>(p);
-        }
-        err = cudaGetLastError();
+        auto go = [&](auto kern, const LaunchInfo& li) {
+            if (li.grid <= 0) return cudaErrorInvalidConfiguration;
+            if (!p.early_start) {
+                kern<<<li.grid, kThreads, li.smem, stream>>>(p);
+                return cudaGetLastError();
+            }
+            // programmatic stream serialisation: the launch may begin before the kernel ahead of
+            // it completes; the kernel's griddepcontrol.wait orders its dependent reads and writes
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)li.grid);
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = li.smem;
+            cfg.stream = stream;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            return cudaLaunchKernelEx(&cfg, kern, p);
+        };
+        if (p.cache_dtype == kBF16) err = go(decode_tc_kernel<kD, __nv_bfloat16>, launch_info<kD, __nv_bfloat16>(device));
+        else err = go(decode_tc_kernel<kD, __half>, launch_info<kD, __half>(device));
     });
     return err;
 }

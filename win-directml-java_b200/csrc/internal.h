@@ -51,6 +51,10 @@ struct DecodeParams {
     const float* q_bias;
     const float* k_bias;
     const float* v_bias;
+    // 1: launched with programmatic stream serialisation: the plan and the first piece's cache
+    // tiles may overlap the kernel before it on the stream, which must not write ctx_lens or
+    // the cache rows below ctx_lens[b] (tensor-core decode only)
+    int early_start;
     double inv_freq[kMaxHeadDim / 2];
 };
 __host__ __device__ inline int64_t q_stride_of(const DecodeParams& p) {
