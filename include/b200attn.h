@@ -129,7 +129,9 @@ B2A_API int b2a_set_workspace_limit(b2a_context* ctx, size_t bytes);
  * k/v rows, biases or norm weights and before any write.  Contract: the kernel launched
  * immediately before a decode on the same stream must not write ctx_lens or the cache
  * rows below ctx_lens[b] (rows the decode reads) -- true of back-to-back decode layers and
- * of projections that produce q / k / v.  Returns B2A_OK, or B2A_EINVAL for a null context. */
+ * of projections that produce q / k / v.  The two projections of b2a_decode_attention_block are
+ * launched the same way: each requests its first weight panels before waiting for the kernel
+ * ahead (which must not write the weights).  Returns B2A_OK, or B2A_EINVAL for a null context. */
 B2A_API int b2a_set_decode_early_start(b2a_context* ctx, int enable);
 
 /* Bytes of device workspace the context currently holds. */

@@ -143,3 +143,17 @@ def test_decode_attention_block_config_batch_bf16(ctx):
     """configs[2]'s batch of 64 with its context lengths (U[512, 8192]), bf16 activations."""
     lens = oracle.splitmix_uniform_int(3, 64, 512, 8192)
     _block_case(ctx, B=64, hidden=896, Hq=14, Hkv=2, D=64, max_seq=8193, lens=lens, dtype=oracle.BF16, seed=940)
+
+
+def test_decode_attention_block_early_start(ctx):
+    """Under b2a_set_decode_early_start the block's QKV GEMM, decode and O GEMM are launched with
+    programmatic serialisation (each GEMM requests its weight panels before waiting for the kernel
+    ahead); two blocks back to back, as two layers, both match the float64 reference."""
+    try:
+        ctx.set_decode_early_start(True)
+        _block_case(ctx, B=6, hidden=896, Hq=14, Hkv=2, D=64, max_seq=2000, lens=[0, 1, 700, 1999, 64, 1500],
+                    dtype=oracle.F16, seed=950)
+        lens = oracle.splitmix_uniform_int(3, 64, 512, 8192)
+        _block_case(ctx, B=64, hidden=896, Hq=14, Hkv=2, D=64, max_seq=8193, lens=lens, dtype=oracle.BF16, seed=960)
+    finally:
+        ctx.set_decode_early_start(False)

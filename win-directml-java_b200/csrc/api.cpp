@@ -973,8 +973,11 @@ B2A_API int b2a_gemma_fused_attention_context(b2a_context* ctx, const float* q, 
 }
 
 // ----------------------------------------------------------------- projections
-B2A_API int b2a_linear(b2a_context* ctx, int in_dtype, int out_dtype, const void* x, const void* w, const float* bias,
-                       const void* residual, void* y, int M, int N, int K, void* stream) {
+namespace {
+// b2a_linear; early: launched with programmatic serialisation (the projections of
+// b2a_decode_attention_block under b2a_set_decode_early_start)
+int run_linear(b2a_context* ctx, int in_dtype, int out_dtype, const void* x, const void* w, const float* bias,
+               const void* residual, void* y, int M, int N, int K, void* stream, bool early) {
     if (!ctx) return B2A_EINVAL;
     if (!x || !w || !y) return fail(ctx, B2A_EINVAL, "x, w and y must not be null");
     if (in_dtype != B2A_FLOAT16 && in_dtype != B2A_BFLOAT16)
@@ -1001,6 +1004,7 @@ B2A_API int b2a_linear(b2a_context* ctx, int in_dtype, int out_dtype, const void
     a.N = N;
     a.K = K;
     a.ksplit = 1;
+    a.early = early ? 1 : 0;
     // launches with too few output tiles to fill the GPU split K over CTAs (without room for the
     // split workspace under the context's limit they run unsplit)
     size_t acc_bytes = 0, counter_ints = 0;
@@ -1022,6 +1026,12 @@ B2A_API int b2a_linear(b2a_context* ctx, int in_dtype, int out_dtype, const void
     const cudaError_t e = launch_linear_tc(a, ctx->status, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(ctx, e, "linear kernel launch");
     return B2A_OK;
+}
+}  // namespace
+
+B2A_API int b2a_linear(b2a_context* ctx, int in_dtype, int out_dtype, const void* x, const void* w, const float* bias,
+                       const void* residual, void* y, int M, int N, int K, void* stream) {
+    return run_linear(ctx, in_dtype, out_dtype, x, w, bias, residual, y, M, N, K, stream, false);
 }
 
 B2A_API int b2a_decode_attention_block(b2a_context* ctx, int act_dtype, int cache_dtype, const void* x,
@@ -1056,7 +1066,8 @@ B2A_API int b2a_decode_attention_block(b2a_context* ctx, int act_dtype, int cach
     float* qkv = static_cast<float*>(ctx->blk_ws);
     void* attn = static_cast<char*>(ctx->blk_ws) + qkv_bytes;
     // 1. qkv = x W_qkv^T + b (fp32 rows [Q | K | V], as the reference keeps them)
-    if ((rc = b2a_linear(ctx, act_dtype, B2A_FLOAT32, x, w_qkv, b_qkv, nullptr, qkv, B, nqkv, hidden, stream)))
+    if ((rc = run_linear(ctx, act_dtype, B2A_FLOAT32, x, w_qkv, b_qkv, nullptr, qkv, B, nqkv, hidden, stream,
+                         ctx->decode_early_start)))
         return rc;
     // 2. RoPE of q and k at ctx_lens[b], k/v append, attention (the decode kernel reads the fused rows)
     DecodeParams p{};
@@ -1096,7 +1107,8 @@ B2A_API int b2a_decode_attention_block(b2a_context* ctx, int act_dtype, int cach
     p.out_dtype = act_dtype;
     if ((rc = run_decode(ctx, p, s, true))) return rc;
     // 3. y = attn W_o^T + residual
-    return b2a_linear(ctx, act_dtype, act_dtype, attn, w_o, nullptr, residual, y, B, hidden, Hq * D, stream);
+    return run_linear(ctx, act_dtype, act_dtype, attn, w_o, nullptr, residual, y, B, hidden, Hq * D, stream,
+                      ctx->decode_early_start);
 }
 
 // ----------------------------------------------------------------- sharding

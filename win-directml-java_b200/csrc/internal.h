@@ -203,6 +203,9 @@ struct LinearArgs {
     int ksplit;
     float* acc;
     int* counters;
+    // early start (programmatic stream serialisation): the weight panels of the first stages are
+    // requested before waiting for the kernel ahead, which must not write w
+    int early;
 };
 bool linear_tc_supported(int in_dtype, int K, int64_t ldx, int64_t ldw, const void* x, const void* w);
 // K ranges per output tile for a launch that leaves SMs idle (1: no split), and its workspace.

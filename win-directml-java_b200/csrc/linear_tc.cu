@@ -63,6 +63,7 @@ struct LinParams {
     int panels_per_split;  // K panels (64 columns) per range
     float* acc;            // split-K: fp32 [M][N] accumulator, zero between launches
     int* counters;         // split-K: [tiles], zero between launches
+    int early;             // launched with programmatic serialisation: wait before reading x / residual
 };
 
 __device__ __forceinline__ float lin_load(const void* p, int64_t i, int dtype) { return load_as_float(p, i, dtype); }
@@ -81,6 +82,9 @@ __global__ void __launch_bounds__(kLThreads, 1)
     linear_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ LinParams p) {
     using Gm = LinGeo<BN>;
+    // a decode launched after this GEMM with early start (b2a_set_decode_early_start) may be
+    // scheduled from now on: it waits for this grid's completion before reading its output
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ unsigned char smem_raw[];
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     unsigned char* base_ptr = smem_raw + (base - smem_u32(smem_raw));
@@ -127,12 +131,22 @@ __global__ void __launch_bounds__(kLThreads, 1)
         // ---------------------------------------------------------------- producer
         if (lane == 0) {
             int issued = 0;
+            // early start: the weight panels of the first stages are requested while the kernel
+            // ahead (which produces x) finishes; each stage's barrier expects x and w bytes alike
+            const int pre = p.early ? min(nk, kLStages) : 0;
+            for (int kt = 0; kt < pre; ++kt) {
+                mbar_expect_tx(bFull(kt), Gm::kStage);
+                tma_load_2d(sW(kt), &tmW, bFull(kt), (kt0 + kt) * kLBK, n0);
+            }
+            if (p.early) asm volatile("griddepcontrol.wait;" ::: "memory");
             for (int kt = 0; kt < nk; ++kt) {
                 const int st = kt % kLStages;
                 if (kt >= kLStages && !mbar_wait(bEmpty(st), ((kt / kLStages) - 1) & 1, abort_flag, status)) break;
-                mbar_expect_tx(bFull(st), Gm::kStage);
+                if (kt >= pre) {
+                    mbar_expect_tx(bFull(st), Gm::kStage);
+                    tma_load_2d(sW(st), &tmW, bFull(st), (kt0 + kt) * kLBK, n0);
+                }
                 tma_load_2d(sX(st), &tmX, bFull(st), (kt0 + kt) * kLBK, m0);
-                tma_load_2d(sW(st), &tmW, bFull(st), (kt0 + kt) * kLBK, n0);
                 issued = kt + 1;
             }
             // every copy issued lands before the CTA may exit
@@ -168,6 +182,7 @@ __global__ void __launch_bounds__(kLThreads, 1)
     __syncwarp();
     const bool ok = __all_sync(0xffffffffu, mbar_wait(bDone, 0, abort_flag, status));
     tc_fence_after();
+    if (p.early) asm volatile("griddepcontrol.wait;" ::: "memory");  // before reading residual / bias, writing
     constexpr int kPitch = 36;  // staged row pitch (floats): 16-byte aligned, conflict-free float4 writes
     float* const stage = reinterpret_cast<float*>(base_ptr);  // the ring is idle once every MMA is done
     const int rows = min(kLBM, p.M - m0);
@@ -392,9 +407,23 @@ cudaError_t launch_linear_tc(const LinearArgs& a, int* status, cudaStream_t stre
     p.panels_per_split = (nk + p.ksplit - 1) / p.ksplit;
     p.acc = a.acc;
     p.counters = a.counters;
+    p.early = a.early;
     const dim3 grid((unsigned)((a.M + kLBM - 1) / kLBM), (unsigned)((a.N + kLinBN - 1) / kLinBN), (unsigned)p.ksplit);
-    linear_tc_kernel<kLinBN><<<grid, kLThreads, LinGeo<kLinBN>::kBytes + 1024, stream>>>(mx, mw, p);
-    return cudaGetLastError();
+    if (!a.early) {
+        linear_tc_kernel<kLinBN><<<grid, kLThreads, LinGeo<kLinBN>::kBytes + 1024, stream>>>(mx, mw, p);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kLThreads);
+    cfg.dynamicSmemBytes = LinGeo<kLinBN>::kBytes + 1024;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, linear_tc_kernel<kLinBN>, mx, mw, p);
 }
 
 }  // namespace b2a
