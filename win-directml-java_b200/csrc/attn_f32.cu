@@ -99,6 +99,10 @@ template <int D>
 __global__ void __launch_bounds__(F32Geo<D>::kThreads) attn_f32_kernel(const __grid_constant__ AttnParams p) {
     using Gm = F32Geo<D>;
     constexpr int kKP = Gm::kKP, kVP = Gm::kVP, kParts = Gm::kParts, kThreads = Gm::kThreads;
+    // launched with programmatic serialisation: placed while the kernel ahead finishes, every global
+    // access waits for it
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     constexpr int kHalfD = D / 2;
     extern __shared__ __align__(16) float fsm[];
     const int tid = threadIdx.x, part = tid >> 7, ht = tid & (kGroup - 1);
@@ -427,9 +431,17 @@ cudaError_t launch_d(const AttnParams& p, cudaStream_t stream) {
         attr[dev] = cudaFuncSetAttribute(attn_f32_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     });
     if (attr[dev] != cudaSuccess) return attr[dev];
-    const dim3 grid((p.S + kBM - 1) / kBM, p.Hq, p.B);
-    attn_f32_kernel<D><<<grid, F32Geo<D>::kThreads, smem, stream>>>(p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((p.S + kBM - 1) / kBM), (unsigned)p.Hq, (unsigned)p.B);
+    cfg.blockDim = dim3(F32Geo<D>::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attn_f32_kernel<D>, p);
 }
 
 }  // namespace

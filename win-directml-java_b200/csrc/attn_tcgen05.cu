@@ -399,6 +399,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     // every use (a 25x slower masked softmax tile when the mask test read them)
     const int n_items = p.n_items;
     int* const status = p.status;
+    // launched with programmatic serialisation: the set-up below (barriers, TMEM) overlaps the
+    // kernel ahead; griddepcontrol.wait follows it, before any global read or write
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (tid == 0) {
         for (int qs = 0; qs < Gm::kQTiles; ++qs) {
@@ -433,6 +436,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp >= 8) {
       asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(RegSplit<D>::kControl));
@@ -1017,11 +1021,20 @@ cudaError_t launch_impl(const AttnParams& a, int* status, cudaStream_t stream, b
                                                   cudaSuccess || sms <= 0)
         return cudaErrorInvalidDevice;
     const dim3 grid((unsigned)std::min(p.n_items, sms));
-    if (additive)
-        attn_tcgen05_kernel<D, true><<<grid, kThreadsTc, smem_request<D>(), stream>>>(mq, mk, mv, p);
-    else
-        attn_tcgen05_kernel<D, false><<<grid, kThreadsTc, smem_request<D>(), stream>>>(mq, mk, mv, p);
-    return cudaGetLastError();
+    // programmatic stream serialisation: the CTAs may be placed, and set up their barriers and
+    // TMEM, while the kernel ahead finishes; they wait for it before touching global memory
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreadsTc);
+    cfg.dynamicSmemBytes = smem_request<D>();
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (additive) return cudaLaunchKernelEx(&cfg, attn_tcgen05_kernel<D, true>, mq, mk, mv, p);
+    return cudaLaunchKernelEx(&cfg, attn_tcgen05_kernel<D, false>, mq, mk, mv, p);
 }
 
 }  // namespace
