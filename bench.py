@@ -572,6 +572,15 @@ def model_step_entry(ctx, torch, name, hbm, time_steps_fn, flush):
 
 
 # ------------------------------------------------------------------ CPU reference arm
+def host_threads() -> int:
+    """Host cores this process may run on.  Passed to the oracle explicitly: torchrun sets
+    OMP_NUM_THREADS=1 in its workers, which would leave the CPU arm on one thread at N > 1."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 class CpuDecodeSample:
     """A bounded sample of the c5 workload for the CPU restatement (OpenMP over all host
     threads): n_seq of the benchmark's 256 sequences, taken at the midpoints of n_seq equal
@@ -599,7 +608,7 @@ class CpuDecodeSample:
         r = lambda *s: oracle.round_to(rng.standard_normal(s, dtype=np.float32), oracle.F16).reshape(s)
         self.q, self.kn, self.vn = r(n_seq, self.Hq, self.D), r(n_seq, self.Hkv, self.D), r(n_seq, self.Hkv, self.D)
         self.w = (0.5 * rng.standard_normal(self.D)).astype(np.float32)
-        self.threads = oracle.max_threads()
+        self.threads = host_threads()
 
     def describe(self) -> str:
         return (f"{self.n} of the 256 sequences (stratified by context length: sample mean "
@@ -654,7 +663,7 @@ def reference_arm(args):
         times.append(time.perf_counter() - t0)
     ms = 1e3 * statistics.mean(times)
     value = smp.n / (ms / 1e3)
-    threads = oracle.max_threads()
+    threads = host_threads()
     sh = DECODE_SHAPES["c5"]
     config = dict(decode_config("c5", sh["B"], synthetic.uniform_int(5, sh["B"] * args.gpus, sh["lo"], sh["hi"]),
                                 sh["hi"] + 1), parallelism=f"shard{args.gpus} (sequences per rank)")
