@@ -703,9 +703,6 @@ B2A_API int b2a_prefill_gemma(b2a_context* ctx, int in_dtype, int out_dtype, con
     auto r256 = [](size_t x) { return (x + 255) / 256 * 256; };
     const bool rope = rope_mode != B2A_ROPE_NONE;
     const bool conv = cdt != in_dtype;
-    // the vectorised pre-pass reads NeoX (cos, sin) rows from the context's cached float table;
-    // Gemma's double table (and the row-wise fallback's) is built per call into the workspace
-    const bool cached_table = rope_mode == B2A_ROPE_NEOX;
     const size_t table_bytes = rope ? r256((size_t)S * (D / 2) * 16) : 0;
     const size_t q_bytes = r256(nq * ce), k_bytes = r256(nk * ce), v_bytes = conv ? r256(nk * ce) : 0;
     rc = ensure_buffer(ctx, &ctx->pf_ws, &ctx->pf_ws_bytes, table_bytes + q_bytes + k_bytes + v_bytes, "prefill");
