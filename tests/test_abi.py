@@ -30,6 +30,8 @@ def test_calls_with_null_context_are_rejected():
                           None, None, 0.0, None, None) == b200attn.B2A_EINVAL
     assert lib.b2a_mha(None, 0, 0, None, None, None, None, None, None, 1, 1, 1, 8, 0.3, 0, None) == \
         b200attn.B2A_EINVAL
+    assert lib.b2a_set_decode_early_start(None, 1) == b200attn.B2A_EINVAL
+    assert lib.b2a_set_workspace_limit(None, 0) == b200attn.B2A_EINVAL
 
 
 def test_create_reports_missing_device_without_crashing():
