@@ -265,6 +265,34 @@ def test_encoder_bf16_beyond_the_fp16_range_is_flagged(ctx):
     assert "fp16 operand range" in str(ei.value)
 
 
+@pytest.mark.parametrize("tensor,value,flagged", [
+    ("q", 65536.0, True),    # rotated at position 0 (identity): rounds to infinity in fp16
+    ("k", -65536.0, True),
+    ("v", 65536.0, True),    # converted without rotation
+    ("v", 65280.0, False),   # the largest bf16 value below fp16's limit stays finite
+    ("q", -65280.0, False),
+])
+def test_prefill_prepass_flags_values_beyond_the_fp16_range(ctx, tensor, value, flagged):
+    """The bf16 pre-pass (RoPE of q, k; conversion of q, k, v to the fp16 operands) raises the device
+    status (B2A_EDEVICE) exactly when a finite value rounds to infinity in fp16."""
+    import torch
+    import b200attn
+    B, S, H, D = 1, 256, 2, 64
+    t = {n: torch.zeros(B, S, H, D, dtype=torch.bfloat16, device="cuda") for n in "qkv"}
+    t[tensor][0, 0, 1, 5] = value
+    y = torch.empty(B, S, H, D, device="cuda")
+    ctx.check_device_status()
+    b200attn.prefill_causal(ctx, t["q"], t["k"], t["v"], y, 0.125, rope_mode=b200attn.ROPE_NEOX, rope_theta=1e4)
+    torch.cuda.synchronize()
+    if not flagged:
+        ctx.check_device_status()
+        return
+    with pytest.raises(b200attn.B200RuntimeException) as ei:
+        ctx.check_device_status()
+    assert ei.value.status == b200attn.B2A_EDEVICE
+    assert "fp16 operand range" in str(ei.value)
+
+
 @pytest.mark.parametrize("dtype,window,theta,S,D", [
     (oracle.BF16, 32, 1e4, 96, 256),    # Gemma-3-270M local layer (4/1 heads, D 256)
     (oracle.BF16, 0, 1e6, 96, 256),     # global layer

@@ -107,6 +107,10 @@ struct PrepParams {
     int* status;
 };
 
+// Out-of-range check (status bit 4 when a finite value rounds to infinity in the 16-bit
+// type): one maximum of the 8 magnitudes against the type's largest finite value; only a
+// group at or above it (rare: values in [max, rounding threshold) still round to a finite
+// value) takes the per-element test.
 __device__ __forceinline__ void store8(void* base, int64_t e, int dtype, const float* x, int* status) {
     if (dtype == kF32) {
         *reinterpret_cast<float4*>(static_cast<float*>(base) + e) = make_float4(x[0], x[1], x[2], x[3]);
@@ -114,23 +118,32 @@ __device__ __forceinline__ void store8(void* base, int64_t e, int dtype, const f
         return;
     }
     uint32_t w[4];
-    bool over = false;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         if (dtype == kBF16) {
             const __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
             w[i] = *reinterpret_cast<const uint32_t*>(&h);
-            const float2 r = __bfloat1622float2(h);
-            over |= (isinf(r.x) && !isinf(x[2 * i])) || (isinf(r.y) && !isinf(x[2 * i + 1]));
         } else {
             const __half2 h = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
             w[i] = *reinterpret_cast<const uint32_t*>(&h);
-            const float2 r = __half22float2(h);
-            over |= (isinf(r.x) && !isinf(x[2 * i])) || (isinf(r.y) && !isinf(x[2 * i + 1]));
+        }
+    }
+    if (status != nullptr) {
+        const float m = fmaxf(fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3]))),
+                              fmaxf(fmaxf(fabsf(x[4]), fabsf(x[5])), fmaxf(fabsf(x[6]), fabsf(x[7]))));
+        if (m >= (dtype == kBF16 ? 3.38953139e38f : 65504.f)) {
+            // per element, on the packed results: infinity in the 16-bit type from a finite input
+            const uint32_t inf16 = dtype == kBF16 ? 0x7F80u : 0x7C00u;
+            bool over = false;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                over |= ((w[i] & 0x7FFFu) == inf16 && !isinf(x[2 * i])) ||
+                        (((w[i] >> 16) & 0x7FFFu) == inf16 && !isinf(x[2 * i + 1]));
+            }
+            if (over) atomicOr(status, 4);
         }
     }
     *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + e) = make_uint4(w[0], w[1], w[2], w[3]);
-    if (over && status != nullptr) atomicOr(status, 4);
 }
 
 // 8 raw elements (16 bytes of a 16-bit type, 32 of fp32), loaded before any
@@ -436,9 +449,10 @@ cudaError_t launch_prep(const PrepJob* jobs, int n_jobs, int B, int S, int D, in
         const int64_t threads = sg.rotate ? sg.units : (sg.units + 2 * heads - 1) / (2 * heads);
         most = threads > most ? threads : most;
     }
-    // 2 blocks of 256 per SM stay resident (about 128 registers a thread); a few passes of the largest segment
+    // 2 blocks of 256 per SM stay resident (about 128 registers a thread): one wave of them loops
+    // over every segment (a grid of several waves measured 256 against 244 us for configs[3])
     const int64_t blocks = (most + 255) / 256;
-    const int grid = (int)(blocks < 148 * 2 * 8 ? blocks : 148 * 2 * 8);
+    const int grid = (int)(blocks < 148 * 2 ? blocks : 148 * 2);
     if (in_dtype != kF32) {
         if (gemma) prep_kernel<2, false, 2><<<grid, 256, 0, stream>>>(p);
         else prep_kernel<1, false, 4><<<grid, 256, 0, stream>>>(p);
