@@ -250,7 +250,7 @@ class DecodeWorkload:
         self.h_vn = [pin(t) for t in self.vn]
         self.h_lens = pin(self.lens_d)
         self.h_out = [torch.empty(B, Hq, D).pin_memory() for _ in self.layers]
-        if world > 1:  # every rank receives the whole batch's outputs of both layers
+        if world > 1:  # every rank receives the whole batch's outputs of both layers; rank 0 copies them out
             from b200attn import sharding
             self.h_out_all = torch.empty(len(self.layers), B * world, Hq, D).pin_memory()
             self.reassemble = sharding.Reassembly(self.plan, torch.device("cuda", torch.cuda.current_device()))
@@ -313,6 +313,8 @@ class DecodeWorkload:
                 self.kn[i].copy_(self.h_kn[i], non_blocking=True)
                 self.vn[i].copy_(self.h_vn[i], non_blocking=True)
                 self.ev_in[i].record(cs)
+        if self.world > 1 and not hasattr(self, "gather_stream"):
+            self.gather_stream = torch.cuda.Stream()
         for i in range(len(self.layers)):
             main.wait_event(self.ev_in[i])
             self.launch(ctx, i)
@@ -321,19 +323,26 @@ class DecodeWorkload:
                 cs.wait_event(self.ev_out[i])
                 with torch.cuda.stream(cs):
                     self.h_out[i].copy_(self.out[i], non_blocking=True)
+            else:
+                # output reassembly per layer on a side stream, so layer i's all-gather and host
+                # copy overlap layer i+1's attention: one NCCL all-gather of the equal shards,
+                # scattered back into unit order; rank 0, the host that consumes the reassembled
+                # batch, copies it out (every rank holds the same reassembled tensor)
+                gs = self.gather_stream
+                gs.wait_event(self.ev_out[i])
+                with torch.cuda.stream(gs):
+                    full = self.reassemble(self.out[i])
+                    if self.rank == 0:
+                        self.h_out_all[i].copy_(full, non_blocking=True)
         if self.world > 1:
-            # output reassembly: one NCCL all-gather of the equal shards (both layers at once),
-            # scattered back into unit order, then the whole batch's outputs to the host
-            local = torch.stack(self.out, dim=1)  # [units, layers, G, D]
-            full = self.reassemble(local)
-            self.h_out_all.copy_(full.transpose(0, 1), non_blocking=True)
+            main.wait_stream(self.gather_stream)
         else:
             self.ev_done.record(cs)
             main.wait_event(self.ev_done)
 
     def e2e_bytes(self):
         h2d = self.lens.nbytes + sum(t.numel() * t.element_size() for t in self.h_q + self.h_kn + self.h_vn)
-        if self.world > 1:
+        if self.world > 1:  # the reassembled batch, copied out once (rank 0)
             d2h = self.h_out_all.numel() * self.h_out_all.element_size()
         else:
             d2h = sum(t.numel() * t.element_size() for t in self.h_out)
@@ -344,7 +353,8 @@ class DecodeWorkload:
         if self.world > 1:
             cfg["partition_unit"] = "(sequence, kv head)" if self.Hkv_model > 1 else "sequence"
             cfg["units_per_rank"] = self.B
-            cfg["reassembly"] = "NCCL all_gather of equal shards in the e2e arm (b200attn.sharding.gather_shards)"
+            cfg["reassembly"] = ("NCCL all_gather of equal shards per layer in the e2e arm, overlapping the next "
+                                 "layer (b200attn.sharding.Reassembly); rank 0 copies the reassembled batch to host")
         return cfg
 
 
