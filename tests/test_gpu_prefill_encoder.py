@@ -239,7 +239,8 @@ def test_prefill_rotated_keys_out_and_rope_modes(ctx, dtype, mode):
     assert np.all(np.abs(got_k - want_k) <= bound), float(np.max(np.abs(got_k - want_k) - bound))
 
 
-@pytest.mark.parametrize("layout,S,D", [(0, 100, 64), (1, 100, 64), (1, 300, 32), (0, 600, 64)])
+@pytest.mark.parametrize("layout,S,D", [(0, 100, 64), (1, 100, 64), (1, 300, 32), (0, 600, 64), (1, 100, 96),
+                                          (0, 300, 96)])
 def test_encoder_bf16_inputs(ctx, layout, S, D):
     """bf16 encoder inputs on the tensor cores: up to 512 keys the kernel converts the staged tiles to
     fp16 itself (its two spare warps); longer sequences go through the conversion pre-pass."""

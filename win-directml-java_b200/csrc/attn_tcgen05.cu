@@ -109,17 +109,24 @@ constexpr int kXformQ = 1, kXformK = 2, kXformV = 4;
 
 template <int D>
 struct TcGeo {
-    static constexpr int NP = (D + 63) / 64;      // 128-byte panels per row
-    static constexpr int kPanelBytes = 128 * 128;  // 128 rows x 128 B
+    // Panels of 64 elements with the 128-byte swizzle; at D = 96, panels of 32 elements with the
+    // 64-byte swizzle: three of them hold a row without padding (a tile takes 24 KB, not 32 KB),
+    // which leaves the shared memory for two Q buffers
+    static constexpr int kPanelElems = D == 96 ? 32 : 64;
+    static constexpr int kRowBytes = 2 * kPanelElems;             // one panel row
+    static constexpr uint32_t kLayout = D == 96 ? 4u : 2u;        // UMMA descriptor layout: 64B / 128B swizzle
+    static constexpr int NP = (D + kPanelElems - 1) / kPanelElems;  // panels per row
+    static constexpr int kPanelBytes = 128 * kRowBytes;          // 128 rows
     static constexpr int kTileBytes = NP * kPanelBytes;
     // query tiles per work item: TMEM holds kTiles x (S 128 + O D) columns, two tiles up to D = 128
     static constexpr int kTiles = D <= 128 ? 2 : 1;
     static constexpr uint32_t kOcol = 128u * kTiles;  // first O column (the S tiles come first)
     // ring stages; at D = 256 one (a step's softmax + 24 MMAs outlast the next tiles' loads)
     static constexpr int kStages = D <= 64 ? 3 : (D <= 128 ? 2 : 1);
-    // Q buffers per tile: two at D <= 64, so that the next work item's Q tiles load while the
-    // current item still reads its own (short items would otherwise wait for Q after every item)
-    static constexpr int kQBuf = D <= 64 ? 2 : 1;
+    // Q buffers per tile: two at D <= 64 and D = 96, so that the next work item's Q tiles load
+    // while the current item still reads its own (short items would otherwise wait for Q after
+    // every item)
+    static constexpr int kQBuf = (D <= 64 || D == 96) ? 2 : 1;
     static constexpr int kQTiles = kQBuf * kTiles;
     static constexpr int oQ = 0;                   // Q tiles: buffer-major, tile-minor
     static constexpr int oK = kQTiles * kTileBytes;
@@ -148,18 +155,23 @@ __device__ __forceinline__ uint4 pack8_f16(const float* x) {
     return u;
 }
 
-// In-kernel conversion of one staged bf16 tile (TMA layout: 128 rows of 64-element, 128-byte-
-// swizzled panels): rows [0, rows) become fp16 in place.  Thread tx of the 64 takes rows tx and
-// tx + 64.  Returns the largest |value| (a value beyond the fp16 range becomes infinite: the
-// caller flags it).
+// In-kernel conversion of one staged bf16 tile (TMA layout: 128 rows of swizzled panels, TcGeo<D>:
+// 64-element panels with the 128-byte swizzle, 32-element ones with the 64-byte swizzle at D = 96):
+// rows [0, rows) become fp16 in place.  Thread tx of the 64 takes rows tx and tx + 64.  Returns the
+// largest |value| (a value beyond the fp16 range becomes infinite: the caller flags it).
 template <int D>
 __device__ __forceinline__ float xform_tile(unsigned char* tile, int tx, int rows) {
-    constexpr int kChunks = D / 8;  // 16-byte chunks of a row that hold data
+    constexpr int kChunks = D / 8;                      // 16-byte chunks of a row that hold data
+    constexpr int kPer = (D == 96 ? 32 : 64) / 8;       // chunks per panel row
+    constexpr int kPanel = 128 * 16 * kPer;             // panel bytes
     float mx = 0.f;
     for (int rr = tx; rr < rows && rr < 128; rr += 64) {
+        // 128-byte swizzle: chunk ^ (row & 7); 64-byte swizzle: chunk ^ ((row >> 1) & 3)
+        const int sw = kPer == 8 ? (rr & 7) : ((rr >> 1) & 3);
 #pragma unroll 4
         for (int c = 0; c < kChunks; ++c) {
-            uint4* pc = reinterpret_cast<uint4*>(tile + (c >> 3) * 16384 + rr * 128 + (((c & 7) ^ (rr & 7)) << 4));
+            uint4* pc = reinterpret_cast<uint4*>(tile + (c / kPer) * kPanel + rr * 16 * kPer +
+                                                 (((c % kPer) ^ sw) << 4));
             float x[8];
             unpack8_bf16(*pc, x);
 #pragma unroll
@@ -490,7 +502,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                     }
                     mbar_expect_tx(bQfull(qs), Gm::kTileBytes);
                     for (int pn = 0; pn < NP; ++pn)
-                        tma_load_4d(sQ + qs * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmQ, bQfull(qs), 64 * pn,
+                        tma_load_4d(sQ + qs * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmQ, bQfull(qs),
+                                    Gm::kPanelElems * pn,
                                     t ? it.h1 : it.h, t ? it.q0b : it.q0a, t ? it.b1 : it.b);
                 }
                 if (!ok) break;
@@ -516,8 +529,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                         const uint32_t dst_a = (i == 0 ? sK : sV) + st * Gm::kTileBytes;
                         const uint32_t dst_b = (i == 0 ? sV : sK) + st * Gm::kTileBytes;
                         for (int pn = 0; pn < NP; ++pn) {
-                            tma_load_4d(dst_a + pn * Gm::kPanelBytes, m, bKVfull(st), 64 * pn, kvh, 0, it.b);
-                            if (two) tma_load_4d(dst_b + pn * Gm::kPanelBytes, m, bKVfull(st), 64 * pn, kvh1, 0, it.b1);
+                            tma_load_4d(dst_a + pn * Gm::kPanelBytes, m, bKVfull(st), Gm::kPanelElems * pn, kvh, 0,
+                                        it.b);
+                            if (two)
+                                tma_load_4d(dst_b + pn * Gm::kPanelBytes, m, bKVfull(st), Gm::kPanelElems * pn, kvh1,
+                                            0, it.b1);
                         }
                         ++g;
                         continue;
@@ -526,12 +542,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                     mbar_expect_tx(bKVfull(st), (has_k ? Gm::kTxTile : 0u) + (has_v ? Gm::kTxTile : 0u));
                     if (has_k)
                         for (int pn = 0; pn < NP; ++pn)
-                            tma_load_4d(sK + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmK, bKVfull(st), 64 * pn,
-                                        kvh, (it.t_begin + i) * kBN, it.b);
+                            tma_load_4d(sK + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmK, bKVfull(st),
+                                        Gm::kPanelElems * pn, kvh, (it.t_begin + i) * kBN, it.b);
                     if (has_v)
                         for (int pn = 0; pn < NP; ++pn)
-                            tma_load_4d(sV + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmV, bKVfull(st), 64 * pn,
-                                        kvh, (it.t_begin + i - 1) * kBN, it.b);
+                            tma_load_4d(sV + st * Gm::kTileBytes + pn * Gm::kPanelBytes, &tmV, bKVfull(st),
+                                        Gm::kPanelElems * pn, kvh, (it.t_begin + i - 1) * kBN, it.b);
                     ++g;
                 }
                 if (!ok) break;
@@ -634,14 +650,15 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
             };
             // descriptors of each buffer's start: a K step, tile or stage offset only moves the
             // 14-bit start-address field (addr >> 4) of the low word, and every offset here stays inside it
-            const uint64_t dQ = smem_desc(sQ, 16, 1024), dK = smem_desc(sK, 16, 1024);
-            const uint64_t dV = smem_desc(sV, Gm::kPanelBytes, 1024);
+            constexpr uint32_t kSbo = 8 * Gm::kRowBytes;  // 8-row core-matrix groups
+            const uint64_t dQ = smem_desc(sQ, 16, kSbo, Gm::kLayout), dK = smem_desc(sK, 16, kSbo, Gm::kLayout);
+            const uint64_t dV = smem_desc(sV, Gm::kPanelBytes, kSbo, Gm::kLayout);
             const uint32_t q_lo = (uint32_t)dQ, v_lo = (uint32_t)dV;
             const uint32_t qk_hi = (uint32_t)(dQ >> 32), v_hi = (uint32_t)(dV >> 32);  // dK's high word is dQ's
             // packed items: tile B's K sits in the V slot (read K-major) and its V in the K slot (read MN-major)
             const bool packed = Gm::kTiles == 2 && p.packed != 0;
-            const uint32_t k_lo_b = packed ? (uint32_t)smem_desc(sV, 16, 1024) : (uint32_t)dK;
-            const uint32_t v_lo_b = packed ? (uint32_t)smem_desc(sK, Gm::kPanelBytes, 1024) : v_lo;
+            const uint32_t k_lo_b = packed ? (uint32_t)smem_desc(sV, 16, kSbo, Gm::kLayout) : (uint32_t)dK;
+            const uint32_t v_lo_b = packed ? (uint32_t)smem_desc(sK, Gm::kPanelBytes, kSbo, Gm::kLayout) : v_lo;
             const uint32_t k_lo = (uint32_t)dK;
             // S_t = Q_t K^T with K in ring stage st
             int qb = 0;  // Q buffer of the current item
@@ -651,20 +668,23 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 const uint32_t d = tmem + 128u * t;
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ++ks) {
-                    const uint32_t koff = ((uint32_t)(ks >> 2) * Gm::kPanelBytes + (uint32_t)(ks & 3) * 32u) >> 4;
+                    constexpr int kSteps = Gm::kPanelElems / 16;  // 16-element K steps per panel
+                    const uint32_t koff =
+                        ((uint32_t)(ks / kSteps) * Gm::kPanelBytes + (uint32_t)(ks % kSteps) * 32u) >> 4;
                     if (ks == 0) umma_ss_w<0>(ln, d, a0, qk_hi, b0, qk_hi, idq);
                     else umma_ss_w<1>(ln, d, a0 + koff, qk_hi, b0 + koff, qk_hi, idq);
                 }
                 umma_commit_w(ln, bSfull(t));
             };
-            // O_t (+)= P_t V with V in ring stage st, MN-major: 8-key atoms 1024 B apart (SBO),
-            // 64-column panels kPanelBytes apart (LBO)
+            // O_t (+)= P_t V with V in ring stage st, MN-major: 8-key atoms 8 panel rows apart (SBO),
+            // panels kPanelBytes apart (LBO); a 16-key step moves 16 panel rows
             auto issue_pv = [&](int t, int st, uint32_t acc) {
                 const uint32_t b0 = (t ? v_lo_b : v_lo) + (uint32_t)(st * Gm::kTileBytes >> 4);
                 const uint32_t d = tmem + Gm::kOcol + 128u * t, a = tmem + 128u * t;
                 umma_ts_w<-1>(ln, d, a, b0, v_hi, idp, acc);
 #pragma unroll
-                for (int kk = 1; kk < kBN / 16; ++kk) umma_ts_w<1>(ln, d, a + kk * 8u, b0 + kk * 128u, v_hi, idp);
+                for (int kk = 1; kk < kBN / 16; ++kk)
+                    umma_ts_w<1>(ln, d, a + kk * 8u, b0 + kk * (uint32_t)Gm::kRowBytes, v_hi, idp);
             };
             for (int k = 0; ok; ++k) {
                 const int slot = k & 1;
@@ -925,12 +945,14 @@ bool make_map(CUtensorMap* m, const void* ptr, int fmt, int B, int S, int H, int
     if (!fn) return false;
     const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
     const cuuint64_t strides[3] = {(cuuint64_t)sh * 2, (cuuint64_t)ss * 2, (cuuint64_t)sb * 2};
-    const cuuint32_t box[4] = {64, 1, 128, 1};
+    // the kernel's panels (TcGeo<D>): 32 elements with the 64-byte swizzle at D = 96, else 64 with the 128-byte one
+    const bool narrow = D == 96;
+    const cuuint32_t box[4] = {narrow ? 32u : 64u, 1, 128, 1};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     const CUresult r = fn(m, fmt ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
                           const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                          narrow ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
