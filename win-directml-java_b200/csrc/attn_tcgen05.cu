@@ -804,10 +804,19 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 #pragma unroll
                 for (int c = 0; c < kBN / 32; ++c) tmem_ld32(s_addr + 32 * c, r + 32 * c);
                 tmem_wait_ld();
+                // scaled: the row holds log2-domain scores (else raw ones, scaled in the max and exponent)
+                bool scaled = false;
                 if (edge) {
-                    // masked tiles become log2-domain scores (-inf outside the row's keys)
+                    // masked tiles: -inf outside the row's keys
                     const int lo = row_lo - n0, hi = row_hi - n0;
-                    if (additive) {
+                    scaled = true;
+                    if (!additive && !uniform && lo <= 0) {
+                        // only an upper bound (key padding, the causal diagonal): one compare per score,
+                        // raw scores kept like an interior tile's
+                        scaled = false;
+#pragma unroll
+                        for (int i = 0; i < kBN; ++i) r[i] = i < hi ? r[i] : __float_as_uint(-INFINITY);
+                    } else if (additive) {
                         const float* mrow = mrow0 + n0;
 #pragma unroll
                         for (int i = 0; i < kBN; ++i)
@@ -830,7 +839,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                     mx3 = max3f(mx3, __uint_as_float(r[i + 6]), __uint_as_float(r[i + 7]));
                 }
                 float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-                if (!edge) mx *= sl2;
+                if (!scaled) mx *= sl2;
                 // lazy rescale: move the reference maximum only when it grew by > threshold;
                 // O is multiplied after pass 2, when the score row no longer holds registers
                 const bool need = mx > m_run + kRescaleThreshold;
@@ -844,7 +853,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                 }
                 const float mb = m_run == -INFINITY ? 0.f : m_run;
                 // pass 2: P = 2^(s - m) as fp16 pairs over the first 64 S columns, row sum
-                const float mul = edge ? 1.f : sl2;
+                const float mul = scaled ? 1.f : sl2;
                 const f32x2 mul2 = f2_make(mul, mul), nmb2 = f2_make(-mb, -mb);
                 f32x2 sum0 = 0ull, sum1 = 0ull;
                 uint32_t pk[kBN / 2];
